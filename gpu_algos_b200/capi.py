@@ -1,0 +1,135 @@
+"""ctypes binding of ``libglm_b200.so`` (the C ABI declared in ``include/glm_b200.h``).
+
+Every function here takes raw device pointers (integers) and sizes, calls
+the library and raises :class:`GlmbError` on a non-zero status.  The
+library must have been built (``python -c "import __graft_entry__ as g;
+g.build()"`` or ``make -C gpu_algos_b200``); importing this module without
+it raises immediately -- there is no host fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libglm_b200.so")
+
+GLMB_OK = 0
+GLMB_ERR_INVALID_VALUE = 1001
+GLMB_ERR_WORKSPACE = 1002
+GLMB_ERR_UNSUPPORTED = 1003
+GLMB_ERR_TOO_LARGE = 1004
+
+GRAD_REGULARIZE = 0x1
+GRAD_WRITE_YHAT = 0x2
+GRAD_Y_ZERO = 0x4
+
+#: the eleven element types of the reference mains, by C-ABI suffix
+SUFFIXES = ("f16", "f32", "f64", "i8", "i16", "i32", "i64", "u8", "u16", "u32", "u64")
+FLOATING = ("f32", "f64")
+
+
+class GlmbError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        self.status = int(status)
+        super().__init__(f"{where}: status {status} ({status_string(status)})")
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_D = ctypes.c_double
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+_SZ = ctypes.c_size_t
+_INT = ctypes.c_int
+
+_lib: ctypes.CDLL | None = None
+
+
+def _declare(L: ctypes.CDLL) -> None:
+    L.glmb_version.restype = _INT
+    L.glmb_status_string.restype = ctypes.c_char_p
+    L.glmb_status_string.argtypes = [_INT]
+    L.glmb_launch_count.restype = _U64
+    L.glmb_last_path.restype = ctypes.c_char_p
+    for s in SUFFIXES:
+        f = getattr(L, f"glmb_predict_{s}")
+        f.argtypes = [_P, _P, _P, _I64, _I64, _I64, _I64, _P]
+        f.restype = _INT
+        f = getattr(L, f"glmb_gradient_workspace_size_{s}")
+        f.argtypes = [_I64, _I64, _I64, _I64]
+        f.restype = _SZ
+        f = getattr(L, f"glmb_gradient_{s}")
+        f.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P, _SZ, _P]
+        f.restype = _INT
+    for s in FLOATING:
+        sig = {
+            "glmb_gradient_partial": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _U32, _P, _SZ, _P],
+            "glmb_gradient_finalize": [_P, _P, _P, _I64, _I64, _I64, _D, _D, _U32, _P],
+            "glmb_prox_step": [_P, _P, _I64, _D, _D, _P],
+            "glmb_prox_update": [_P, _P, _P, _I64, _I64, _I64, _D, _D, _P],
+            "glmb_power_step": [_P, _P, _P, _P, _I64, _I64, _D, _P],
+            "glmb_power_init": [_P, _I64, _I64, _U64, _P],
+            "glmb_fit_elastic_net": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _INT, _INT,
+                                     _U64, _P, _SZ, _P],
+        }
+        for name, args in sig.items():
+            f = getattr(L, f"{name}_{s}")
+            f.argtypes = args
+            f.restype = _INT
+        f = getattr(L, f"glmb_fit_workspace_size_{s}")
+        f.argtypes = [_I64, _I64, _I64, _I64]
+        f.restype = _SZ
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `make -C gpu_algos_b200` "
+                "(the GLM path has no host fallback)")
+        _lib = ctypes.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().glmb_status_string(int(status)).decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != GLMB_OK:
+        raise GlmbError(status, where)
+
+
+def version() -> int:
+    return int(lib().glmb_version())
+
+
+def launch_count() -> int:
+    return int(lib().glmb_launch_count())
+
+
+def last_path() -> str:
+    return lib().glmb_last_path().decode()
+
+
+def call(name: str, *args) -> int:
+    """Call ``name`` with ``args`` and raise on a non-zero status."""
+    st = getattr(lib(), name)(*args)
+    check(st, name)
+    return st
+
+
+def exported_symbols() -> list[str]:
+    """Every entry point declared in include/glm_b200.h (for the load test)."""
+    names = ["glmb_version", "glmb_status_string", "glmb_launch_count", "glmb_last_path"]
+    for s in SUFFIXES:
+        names += [f"glmb_predict_{s}", f"glmb_gradient_workspace_size_{s}", f"glmb_gradient_{s}"]
+    for s in FLOATING:
+        names += [f"glmb_gradient_partial_{s}", f"glmb_gradient_finalize_{s}", f"glmb_prox_step_{s}",
+                  f"glmb_prox_update_{s}", f"glmb_power_step_{s}", f"glmb_power_init_{s}",
+                  f"glmb_fit_workspace_size_{s}", f"glmb_fit_elastic_net_{s}"]
+    return names

@@ -1,0 +1,399 @@
+// glm_capi.cu -- the extern "C" entry points declared in include/glm_b200.h.
+//
+// Each entry point validates its arguments, picks a kernel family and
+// launches asynchronously on the caller's stream:
+//   - "rows":    fused single-pass kernel (glm_rows.cuh) for float/double
+//                when ntargets <= 8 and the per-lane accumulators fit in
+//                registers (nfeatures up to 1024 for float, 256 for double
+//                with a single target);
+//   - "generic": two-pass kernels (glm_generic.cu) for every other shape and
+//                for half and integer types.
+// Nothing here falls back to the host: a missing or failing device returns
+// the CUDA error code.
+#include <cstring>
+#include <mutex>
+
+#include "glm_common.cuh"
+#include "glm_fit.cuh"
+#include "glm_generic.cuh"
+#include "glm_rows.cuh"
+
+namespace glmb {
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+thread_local const char* g_last_path = "none";
+
+struct DeviceInfo {
+    int sm = 0;
+    int major = 0;
+};
+DeviceInfo g_devices[64];
+std::mutex g_dev_mutex;
+
+int device_info(DeviceInfo* out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return int(e);
+    if (dev < 0 || dev >= 64) return GLMB_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    DeviceInfo& d = g_devices[dev];
+    if (d.sm == 0) {
+        if ((e = cudaDeviceGetAttribute(&d.sm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return int(e);
+        if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+            return int(e);
+    }
+    *out = d;
+    return GLMB_OK;
+}
+}  // namespace
+
+void count_launch(int n) { g_launches.fetch_add(uint64_t(n), std::memory_order_relaxed); }
+void set_last_path(const char* path) { g_last_path = path; }
+
+int sm_count() {
+    DeviceInfo d;
+    return device_info(&d) == GLMB_OK && d.sm > 0 ? d.sm : 148;
+}
+
+namespace {
+
+// The library carries sm_100a code only.
+int check_device() {
+    DeviceInfo d;
+    const int st = device_info(&d);
+    if (st != GLMB_OK) return st;
+    return d.major == 10 ? GLMB_OK : GLMB_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+struct Native {
+    using type = T;
+};
+template <>
+struct Native<uint16_t> {
+    using type = uint16_t;
+};
+
+template <typename T>
+constexpr bool kRowsType = std::is_same_v<T, float> || std::is_same_v<T, double>;
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T>
+int predict_impl(const T* X, const T* M, T* Yhat, int64_t nf, int64_t nt, int64_t ntasks,
+                 int64_t nobs, cudaStream_t stream) {
+    if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0) return GLMB_ERR_INVALID_VALUE;
+    const int64_t nout = nt * ntasks * nobs;
+    if (nout == 0) return GLMB_OK;
+    if (Yhat == nullptr) return GLMB_ERR_INVALID_VALUE;
+    int st = check_device();
+    if (st != GLMB_OK) return st;
+    if (nf == 0) {
+        set_last_path("memset");
+        return int(cudaMemsetAsync(Yhat, 0, size_t(nout) * sizeof(T), stream));
+    }
+    if (X == nullptr || M == nullptr) return GLMB_ERR_INVALID_VALUE;
+    if constexpr (kRowsType<T>) {
+        const RowsPlan p = rows_plan<T>(nf, nt, ntasks, nobs, aligned16(X), false);
+        if (p.ok) {
+            RowsArgs a{X, M, nullptr, Yhat, nullptr, nf, nt, ntasks, nobs, p.obs_per_cta,
+                       p.ctas_per_task, p.seg_log2};
+            set_last_path("rows");
+            return rows_launch<T>(p, kRowsPredict, a, stream);
+        }
+    }
+    set_last_path("generic");
+    return generic_predict<T>(X, M, Yhat, nf, nt, ntasks, nobs, stream);
+}
+
+template <typename T>
+size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
+    if (nf <= 0 || nt <= 0 || ntasks <= 0 || nobs < 0) return 0;
+    if (check_device() != GLMB_OK) return 0;
+    size_t need = 0;
+    bool all_rows = false;
+    if constexpr (kRowsType<T>) {
+        const RowsPlan a = rows_plan<T>(nf, nt, ntasks, nobs, true, true);
+        const RowsPlan b = rows_plan<T>(nf, nt, ntasks, nobs, false, true);
+        all_rows = a.ok && b.ok;
+        if (a.ok) need = std::max(need, round_up(a.part_doubles * sizeof(double), 256));
+        if (b.ok) need = std::max(need, round_up(b.part_doubles * sizeof(double), 256));
+    }
+    if (!all_rows) need = std::max(need, generic_workspace_bytes<T>(nf, nt, ntasks, nobs));
+    return need;
+}
+
+// Shared body of glmb_gradient_* (partial_out == NULL) and
+// glmb_gradient_partial_* (partial_out != NULL, grad unused).
+template <typename T>
+int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
+                  int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda, double alpha,
+                  uint32_t flags, void* ws, size_t ws_bytes, cudaStream_t stream) {
+    if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0) return GLMB_ERR_INVALID_VALUE;
+    if (flags & ~(GLMB_GRAD_REGULARIZE | GLMB_GRAD_WRITE_YHAT | GLMB_GRAD_Y_ZERO))
+        return GLMB_ERR_INVALID_VALUE;
+    const bool reg = (flags & GLMB_GRAD_REGULARIZE) != 0;
+    const bool write_yhat = (flags & GLMB_GRAD_WRITE_YHAT) != 0;
+    const bool y_zero = (flags & GLMB_GRAD_Y_ZERO) != 0;
+    if (nt == 0 || ntasks == 0) return GLMB_OK;
+    const int64_t nout = nobs * ntasks * nt;
+    if (write_yhat && nout > 0 && Yhat == nullptr) return GLMB_ERR_INVALID_VALUE;
+    int st = check_device();
+    if (st != GLMB_OK) return st;
+    if (nf == 0) {
+        set_last_path("memset");
+        if (write_yhat && nout > 0)
+            return int(cudaMemsetAsync(Yhat, 0, size_t(nout) * sizeof(T), stream));
+        return GLMB_OK;
+    }
+    if (M == nullptr || (partial_out == nullptr && grad == nullptr)) return GLMB_ERR_INVALID_VALUE;
+    if (nobs > 0 && (X == nullptr || (!y_zero && Y == nullptr))) return GLMB_ERR_INVALID_VALUE;
+    const T* Yin = y_zero ? nullptr : Y;
+    T* Yhat_out = write_yhat ? Yhat : nullptr;
+    if constexpr (kRowsType<T>) {
+        const RowsPlan p = rows_plan<T>(nf, nt, ntasks, nobs, aligned16(X), true);
+        if (p.ok) {
+            Scratch sc(ws, ws_bytes, round_up(p.part_doubles * sizeof(double), 256), stream);
+            if (sc.status() != GLMB_OK) return sc.status();
+            RowsArgs a{X, M, Yin, Yhat_out, sc.as<double>(), nf, nt, ntasks, nobs, p.obs_per_cta,
+                       p.ctas_per_task, p.seg_log2};
+            set_last_path("rows");
+            st = rows_launch<T>(p, write_yhat ? kRowsGradYhat : kRowsGrad, a, stream);
+            if (st != GLMB_OK) return st;
+            return finalize_launch<T, double>(sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M,
+                                              grad, partial_out, lambda, alpha, reg, stream);
+        }
+    }
+    set_last_path("generic");
+    return generic_gradient<T>(X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
+                               alpha, reg, ws, ws_bytes, stream);
+}
+
+template <typename T>
+size_t fit_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
+    const size_t grad_ws = std::max(gradient_ws_impl<T>(nf, nt, ntasks, nobs),
+                                    gradient_ws_impl<T>(nf, 1, ntasks, nobs));
+    const size_t part = round_up(size_t(ntasks) * std::max<int64_t>(nt, 1) * nf * sizeof(double), 256);
+    const size_t v = round_up(size_t(ntasks) * nf * sizeof(T), 256);
+    const size_t norm = round_up(size_t(ntasks) * sizeof(double), 256);
+    return grad_ws + part + v + norm;
+}
+
+template <typename T>
+int fit_impl(const T* X, const T* Y, T* beta, double* lipschitz, int64_t nf, int64_t nt,
+             int64_t ntasks, int64_t nobs, double lambda1, double lambda2, int n_power, int n_iter,
+             uint64_t seed, void* ws, size_t ws_bytes, cudaStream_t stream) {
+    if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0 || n_power < 0 || n_iter < 0)
+        return GLMB_ERR_INVALID_VALUE;
+    if (lambda1 < 0 || lambda2 < 0) return GLMB_ERR_INVALID_VALUE;
+    if (nf == 0 || nt == 0 || ntasks == 0) return GLMB_OK;
+    if (beta == nullptr || lipschitz == nullptr) return GLMB_ERR_INVALID_VALUE;
+    if (n_iter > 0 && n_power < 1) return GLMB_ERR_INVALID_VALUE;
+    int st = check_device();
+    if (st != GLMB_OK) return st;
+    const size_t grad_ws = std::max(gradient_ws_impl<T>(nf, nt, ntasks, nobs),
+                                    gradient_ws_impl<T>(nf, 1, ntasks, nobs));
+    Scratch sc(ws, ws_bytes, fit_ws_impl<T>(nf, nt, ntasks, nobs), stream);
+    if (sc.status() != GLMB_OK) return sc.status();
+    char* base = sc.as<char>();
+    void* gws = base;
+    double* part = reinterpret_cast<double*>(base + grad_ws);
+    T* v = reinterpret_cast<T*>(base + grad_ws +
+                                round_up(size_t(ntasks) * nt * nf * sizeof(double), 256));
+    double* norm = reinterpret_cast<double*>(reinterpret_cast<char*>(v) +
+                                             round_up(size_t(ntasks) * nf * sizeof(T), 256));
+    const int64_t K = nt * nf;
+    if ((st = power_init<T>(v, nf, ntasks, seed, stream)) != GLMB_OK) return st;
+    for (int it = 0; it < n_power; ++it) {
+        st = gradient_impl<T>(X, v, nullptr, nullptr, nullptr, part, nf, 1, ntasks, nobs, 0.0, 0.0,
+                              GLMB_GRAD_Y_ZERO, gws, grad_ws, stream);
+        if (st != GLMB_OK) return st;
+        if ((st = power_step<T>(part, v, norm, lipschitz, nf, ntasks, lambda2, stream)) != GLMB_OK)
+            return st;
+    }
+    cudaError_t e = cudaMemsetAsync(beta, 0, size_t(K * ntasks) * sizeof(T), stream);
+    if (e != cudaSuccess) return int(e);
+    for (int it = 0; it < n_iter; ++it) {
+        st = gradient_impl<T>(X, beta, Y, nullptr, nullptr, part, nf, nt, ntasks, nobs, 0.0, 0.0, 0u,
+                              gws, grad_ws, stream);
+        if (st != GLMB_OK) return st;
+        if ((st = prox_update<T>(part, beta, lipschitz, K, ntasks, lambda1, lambda2, stream)) != GLMB_OK)
+            return st;
+    }
+    return GLMB_OK;
+}
+
+// Exceptions (std::bad_alloc from the standard library) never cross the ABI.
+template <typename F>
+int guarded(F&& f) {
+    try {
+        return f();
+    } catch (...) {
+        return GLMB_ERR_INVALID_VALUE;
+    }
+}
+
+}  // namespace
+}  // namespace glmb
+
+using glmb::guarded;
+
+extern "C" {
+
+int glmb_version(void) { return 100; }
+
+const char* glmb_status_string(int status) {
+    switch (status) {
+        case GLMB_OK: return "success";
+        case GLMB_ERR_INVALID_VALUE: return "invalid argument (negative size or NULL pointer)";
+        case GLMB_ERR_WORKSPACE: return "workspace smaller than required";
+        case GLMB_ERR_UNSUPPORTED: return "unsupported device (libglm_b200 carries sm_100a code only)";
+        case GLMB_ERR_TOO_LARGE: return "size beyond a documented limit";
+        default:
+            if (status > 0 && status < 1000) return cudaGetErrorString(static_cast<cudaError_t>(status));
+            return "unknown status";
+    }
+}
+
+uint64_t glmb_launch_count(void) { return glmb::g_launches.load(std::memory_order_relaxed); }
+
+const char* glmb_last_path(void) { return glmb::g_last_path; }
+
+#define GLMB_DEFINE_BASIC(SFX, CT, NT_)                                                            \
+    int glmb_predict_##SFX(const CT* X, const CT* M, CT* Yhat, int64_t nf, int64_t nt,            \
+                           int64_t ntasks, int64_t nobs, glmb_stream_t stream) {                   \
+        return guarded([&] {                                                                       \
+            return glmb::predict_impl<NT_>(reinterpret_cast<const NT_*>(X),                        \
+                                           reinterpret_cast<const NT_*>(M),                        \
+                                           reinterpret_cast<NT_*>(Yhat), nf, nt, ntasks, nobs,     \
+                                           reinterpret_cast<cudaStream_t>(stream));                \
+        });                                                                                        \
+    }                                                                                              \
+    size_t glmb_gradient_workspace_size_##SFX(int64_t nf, int64_t nt, int64_t ntasks,             \
+                                              int64_t nobs) {                                      \
+        try {                                                                                      \
+            return glmb::gradient_ws_impl<NT_>(nf, nt, ntasks, nobs);                              \
+        } catch (...) {                                                                            \
+            return 0;                                                                              \
+        }                                                                                          \
+    }                                                                                              \
+    int glmb_gradient_##SFX(const CT* X, const CT* M, const CT* Y, CT* grad_M, CT* Yhat,          \
+                            int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda,   \
+                            double alpha, uint32_t flags, void* workspace, size_t workspace_bytes, \
+                            glmb_stream_t stream) {                                                \
+        return guarded([&] {                                                                       \
+            return glmb::gradient_impl<NT_>(                                                       \
+                reinterpret_cast<const NT_*>(X), reinterpret_cast<const NT_*>(M),                  \
+                reinterpret_cast<const NT_*>(Y), reinterpret_cast<NT_*>(grad_M),                   \
+                reinterpret_cast<NT_*>(Yhat), nullptr, nf, nt, ntasks, nobs, lambda, alpha, flags, \
+                workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));               \
+        });                                                                                        \
+    }
+
+GLMB_DEFINE_BASIC(f16, uint16_t, __half)
+GLMB_DEFINE_BASIC(f32, float, float)
+GLMB_DEFINE_BASIC(f64, double, double)
+GLMB_DEFINE_BASIC(i8, int8_t, int8_t)
+GLMB_DEFINE_BASIC(i16, int16_t, int16_t)
+GLMB_DEFINE_BASIC(i32, int32_t, int32_t)
+GLMB_DEFINE_BASIC(i64, int64_t, int64_t)
+GLMB_DEFINE_BASIC(u8, uint8_t, uint8_t)
+GLMB_DEFINE_BASIC(u16, uint16_t, uint16_t)
+GLMB_DEFINE_BASIC(u32, uint32_t, uint32_t)
+GLMB_DEFINE_BASIC(u64, uint64_t, uint64_t)
+
+#define GLMB_DEFINE_FLOATING(SFX, T)                                                               \
+    int glmb_gradient_partial_##SFX(const T* X, const T* M, const T* Y, double* partial, T* Yhat, \
+                                    int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,          \
+                                    uint32_t flags, void* workspace, size_t workspace_bytes,       \
+                                    glmb_stream_t stream) {                                        \
+        if (partial == nullptr && nf > 0 && nt > 0 && ntasks > 0) return GLMB_ERR_INVALID_VALUE;   \
+        return guarded([&] {                                                                       \
+            return glmb::gradient_impl<T>(X, M, Y, nullptr, Yhat, partial, nf, nt, ntasks, nobs,   \
+                                          0.0, 0.0, flags & ~GLMB_GRAD_REGULARIZE, workspace,      \
+                                          workspace_bytes, reinterpret_cast<cudaStream_t>(stream)); \
+        });                                                                                        \
+    }                                                                                              \
+    int glmb_gradient_finalize_##SFX(const double* partial, const T* M, T* grad_M, int64_t nf,    \
+                                     int64_t nt, int64_t ntasks, double lambda, double alpha,      \
+                                     uint32_t flags, glmb_stream_t stream) {                       \
+        if (nf < 0 || nt < 0 || ntasks < 0) return GLMB_ERR_INVALID_VALUE;                         \
+        const int64_t total = nf * nt * ntasks;                                                    \
+        if (total == 0) return GLMB_OK;                                                            \
+        if (partial == nullptr || M == nullptr || grad_M == nullptr) return GLMB_ERR_INVALID_VALUE; \
+        return guarded([&] {                                                                       \
+            const int st = glmb::check_device();                                                   \
+            if (st != GLMB_OK) return st;                                                          \
+            return glmb::finalize_launch<T, double>(partial, 1, total, M, grad_M, nullptr, lambda, \
+                                                    alpha, (flags & GLMB_GRAD_REGULARIZE) != 0,    \
+                                                    reinterpret_cast<cudaStream_t>(stream));       \
+        });                                                                                        \
+    }                                                                                              \
+    int glmb_prox_step_##SFX(T* beta, const T* grad_smooth, int64_t n, double inv_L, double l1,   \
+                             glmb_stream_t stream) {                                               \
+        if (n < 0 || inv_L < 0 || l1 < 0) return GLMB_ERR_INVALID_VALUE;                           \
+        if (n > 0 && (beta == nullptr || grad_smooth == nullptr)) return GLMB_ERR_INVALID_VALUE;   \
+        return guarded([&] {                                                                       \
+            return glmb::prox_step<T>(beta, grad_smooth, n, inv_L, l1,                             \
+                                      reinterpret_cast<cudaStream_t>(stream));                     \
+        });                                                                                        \
+    }                                                                                              \
+    int glmb_prox_update_##SFX(const double* partial, T* beta, const double* lipschitz,           \
+                               int64_t nf, int64_t nt, int64_t ntasks, double lambda1,             \
+                               double lambda2, glmb_stream_t stream) {                             \
+        if (nf < 0 || nt < 0 || ntasks < 0 || lambda1 < 0 || lambda2 < 0)                          \
+            return GLMB_ERR_INVALID_VALUE;                                                         \
+        if (nf * nt * ntasks > 0 && (partial == nullptr || beta == nullptr || lipschitz == nullptr)) \
+            return GLMB_ERR_INVALID_VALUE;                                                         \
+        return guarded([&] {                                                                       \
+            return glmb::prox_update<T>(partial, beta, lipschitz, nf * nt, ntasks, lambda1,        \
+                                        lambda2, reinterpret_cast<cudaStream_t>(stream));          \
+        });                                                                                        \
+    }                                                                                              \
+    int glmb_power_step_##SFX(const double* partial, T* v, double* norm, double* lipschitz,       \
+                              int64_t nf, int64_t ntasks, double lambda2, glmb_stream_t stream) {  \
+        if (nf < 0 || ntasks < 0 || lambda2 < 0) return GLMB_ERR_INVALID_VALUE;                    \
+        if (ntasks > 0 && (partial == nullptr || v == nullptr || norm == nullptr ||                \
+                           lipschitz == nullptr))                                                  \
+            return GLMB_ERR_INVALID_VALUE;                                                         \
+        if (ntasks > 0x7fffffff) return GLMB_ERR_TOO_LARGE;                                        \
+        return guarded([&] {                                                                       \
+            return glmb::power_step<T>(partial, v, norm, lipschitz, nf, ntasks, lambda2,           \
+                                       reinterpret_cast<cudaStream_t>(stream));                    \
+        });                                                                                        \
+    }                                                                                              \
+    int glmb_power_init_##SFX(T* v, int64_t nf, int64_t ntasks, uint64_t seed,                    \
+                              glmb_stream_t stream) {                                              \
+        if (nf < 0 || ntasks < 0) return GLMB_ERR_INVALID_VALUE;                                   \
+        if (nf * ntasks > 0 && v == nullptr) return GLMB_ERR_INVALID_VALUE;                        \
+        if (ntasks > 0x7fffffff) return GLMB_ERR_TOO_LARGE;                                        \
+        return guarded([&] {                                                                       \
+            return glmb::power_init<T>(v, nf, ntasks, seed, reinterpret_cast<cudaStream_t>(stream)); \
+        });                                                                                        \
+    }                                                                                              \
+    size_t glmb_fit_workspace_size_##SFX(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {  \
+        try {                                                                                      \
+            return glmb::fit_ws_impl<T>(nf, nt, ntasks, nobs);                                     \
+        } catch (...) {                                                                            \
+            return 0;                                                                              \
+        }                                                                                          \
+    }                                                                                              \
+    int glmb_fit_elastic_net_##SFX(const T* X, const T* Y, T* beta, double* lipschitz,            \
+                                   int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,           \
+                                   double lambda1, double lambda2, int n_power, int n_iter,        \
+                                   uint64_t seed, void* workspace, size_t workspace_bytes,         \
+                                   glmb_stream_t stream) {                                         \
+        if (ntasks > 0x7fffffff) return GLMB_ERR_TOO_LARGE;                                        \
+        return guarded([&] {                                                                       \
+            return glmb::fit_impl<T>(X, Y, beta, lipschitz, nf, nt, ntasks, nobs, lambda1,         \
+                                     lambda2, n_power, n_iter, seed, workspace, workspace_bytes,   \
+                                     reinterpret_cast<cudaStream_t>(stream));                      \
+        });                                                                                        \
+    }
+
+GLMB_DEFINE_FLOATING(f32, float)
+GLMB_DEFINE_FLOATING(f64, double)
+
+}  // extern "C"

@@ -1,0 +1,222 @@
+// glm_common.cuh -- shared device/host helpers of libglm_b200.so (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <type_traits>
+
+#include "glm_b200.h"
+
+namespace glmb {
+
+constexpr int kWarp = 32;
+
+// Kernel launches made by this library (reported by glmb_launch_count).
+void count_launch(int n = 1);
+// Records which kernel family the current call used (glmb_last_path).
+void set_last_path(const char* path);
+
+// SM count of the current device (cached per device).
+int sm_count();
+
+// Status of the last launch, mapped onto the C-ABI status space.
+inline int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? GLMB_OK : static_cast<int>(e);
+}
+
+// ---- storage type <-> arithmetic type --------------------------------------
+//
+// Acc is the type partial sums are carried in.  float inputs carry partials
+// in double (the fused kernels sum short runs in float and spill into
+// double), double stays double, half computes in float, integers compute
+// modulo 2^bits in the unsigned type of the same (or 32-bit) width.
+template <typename T>
+struct Arith;
+template <>
+struct Arith<float> {
+    using Acc = double;
+    using Dot = float;
+};
+template <>
+struct Arith<double> {
+    using Acc = double;
+    using Dot = double;
+};
+template <>
+struct Arith<__half> {
+    using Acc = float;
+    using Dot = float;
+};
+#define GLMB_INT_ARITH(T, U)   \
+    template <>                \
+    struct Arith<T> {          \
+        using Acc = U;         \
+        using Dot = U;         \
+    };
+GLMB_INT_ARITH(int8_t, uint32_t)
+GLMB_INT_ARITH(int16_t, uint32_t)
+GLMB_INT_ARITH(int32_t, uint32_t)
+GLMB_INT_ARITH(int64_t, uint64_t)
+GLMB_INT_ARITH(uint8_t, uint32_t)
+GLMB_INT_ARITH(uint16_t, uint32_t)
+GLMB_INT_ARITH(uint32_t, uint32_t)
+GLMB_INT_ARITH(uint64_t, uint64_t)
+#undef GLMB_INT_ARITH
+
+template <typename A, typename T>
+__device__ __forceinline__ A to_arith(T v) {
+    if constexpr (std::is_same_v<T, __half>) {
+        return static_cast<A>(__half2float(v));
+    } else {
+        return static_cast<A>(v);
+    }
+}
+
+template <typename T, typename A>
+__device__ __forceinline__ T from_arith(A v) {
+    if constexpr (std::is_same_v<T, __half>) {
+        return __float2half_rn(static_cast<float>(v));
+    } else {
+        return static_cast<T>(v);
+    }
+}
+
+// The reference's Number(double) conversion of lambda / alpha.
+template <typename T>
+__host__ __device__ __forceinline__ T from_double(double d) {
+    if constexpr (std::is_same_v<T, __half>) {
+        return __double2half(d);
+    } else {
+        return static_cast<T>(d);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ int sign_of(T v) {
+    // include/cuda/cuda_utils.cuh:475-485 of the reference: is_positive /
+    // is_negative; unsigned values are never negative, sign(0) = 0.
+    if constexpr (std::is_same_v<T, __half>) {
+        const float f = __half2float(v);
+        return f > 0.f ? 1 : (f < 0.f ? -1 : 0);
+    } else if constexpr (std::is_unsigned_v<T>) {
+        return v > T(0) ? 1 : 0;
+    } else {
+        return v > T(0) ? 1 : (v < T(0) ? -1 : 0);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ bool t_gt0(T v) {
+    if constexpr (std::is_same_v<T, __half>) return __half2float(v) > 0.f;
+    else return v > T(0);
+}
+template <typename T>
+__device__ __forceinline__ bool t_lt1(T v) {
+    if constexpr (std::is_same_v<T, __half>) return __half2float(v) < 1.f;
+    else return v < T(1);
+}
+
+// Final value of one gradient element from its sum S = sum (yhat - y) * x,
+// in the reference's host order (glm_gradient_xyyhat.cuh:839-851):
+//   g = 2*S;  if lambda > 0: { if alpha > 0: g += lambda*alpha*sign(M);
+//                              if alpha < 1: g += 2*lambda*(1-alpha)*M }
+// with every constant formed in the Number type.
+template <typename T, typename S>
+__device__ __forceinline__ T finalize_value(S sum, T m, double lambda, double alpha, bool reg) {
+    using A = typename Arith<T>::Dot;
+    A g;
+    if constexpr (std::is_floating_point_v<S> && std::is_same_v<A, float>) {
+        g = static_cast<float>(2.0 * static_cast<double>(sum));
+    } else {
+        g = static_cast<A>(A(2) * static_cast<A>(sum));
+    }
+    if (reg) {
+        const T lam_t = from_double<T>(lambda), alp_t = from_double<T>(alpha);
+        if (t_gt0(lam_t)) {
+            const A lam = to_arith<A>(lam_t), alp = to_arith<A>(alp_t);
+            const A two_lambda = A(2) * lam;
+            const A one_minus_alpha = A(1) - alp;
+            const A two_lambda_one_minus_alpha = two_lambda * one_minus_alpha;
+            const A lambda_alpha = lam * alp;
+            if (t_gt0(alp_t)) g += lambda_alpha * static_cast<A>(sign_of(m));
+            if (t_lt1(alp_t)) g += two_lambda_one_minus_alpha * to_arith<A>(m);
+        }
+    }
+    return from_arith<T>(g);
+}
+
+// ---- global loads that bypass L1 (X is streamed exactly once) -------------
+template <typename T, int VEC>
+struct VecLoad;
+
+template <>
+struct VecLoad<float, 4> {
+    __device__ __forceinline__ static void load(const float* p, float (&v)[4]) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.f32 {%0,%1,%2,%3}, [%4];"
+                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                     : "l"(p));
+    }
+};
+template <>
+struct VecLoad<double, 2> {
+    __device__ __forceinline__ static void load(const double* p, double (&v)[2]) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v2.f64 {%0,%1}, [%2];"
+                     : "=d"(v[0]), "=d"(v[1])
+                     : "l"(p));
+    }
+};
+template <>
+struct VecLoad<float, 1> {
+    __device__ __forceinline__ static void load(const float* p, float (&v)[1]) {
+        asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v[0]) : "l"(p));
+    }
+};
+template <>
+struct VecLoad<double, 1> {
+    __device__ __forceinline__ static void load(const double* p, double (&v)[1]) {
+        asm volatile("ld.global.nc.L1::no_allocate.f64 %0, [%1];" : "=d"(v[0]) : "l"(p));
+    }
+};
+
+// Scratch for one call: either the caller's workspace or a stream-ordered
+// allocation released at the end of the call.
+class Scratch {
+   public:
+    Scratch(void* ws, size_t ws_bytes, size_t need, cudaStream_t s)
+        : stream_(s), need_(need) {
+        if (need == 0) return;
+        if (ws != nullptr) {
+            status_ = ws_bytes >= need ? GLMB_OK : GLMB_ERR_WORKSPACE;
+            ptr_ = ws;
+        } else {
+            const cudaError_t e = cudaMallocAsync(&ptr_, need, s);
+            status_ = e == cudaSuccess ? GLMB_OK : static_cast<int>(e);
+            owned_ = e == cudaSuccess;
+        }
+    }
+    ~Scratch() {
+        if (owned_) cudaFreeAsync(ptr_, stream_);
+    }
+    Scratch(const Scratch&) = delete;
+    Scratch& operator=(const Scratch&) = delete;
+    int status() const { return status_; }
+    template <typename P>
+    P* as() const {
+        return static_cast<P*>(ptr_);
+    }
+
+   private:
+    cudaStream_t stream_;
+    size_t need_;
+    void* ptr_ = nullptr;
+    bool owned_ = false;
+    int status_ = GLMB_OK;
+};
+
+inline size_t round_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+}  // namespace glmb

@@ -1,0 +1,155 @@
+// glm_rows_impl.cuh -- launch planning and dispatch of the rows kernel.
+// Included by glm_rows_f32.cu / glm_rows_f64.cu, one instantiation per file
+// so the two element types compile in parallel.
+#pragma once
+
+#include <algorithm>
+
+#include "glm_rows.cuh"
+
+namespace glmb {
+
+template <typename T>
+constexpr int rows_budget() {
+    // register-resident accumulator words per lane (NT * CPL * VEC)
+    return sizeof(T) == 4 ? 32 : 16;
+}
+
+template <typename T, int VEC, int CPL, int NT>
+constexpr bool rows_valid() {
+    return NT * CPL * VEC <= rows_budget<T>();
+}
+
+// Calls f.template operator()<VEC, CPL, NT>() for the runtime triple.
+template <typename T, typename F>
+int rows_dispatch(int vec, int cpl, int ntmax, F&& f) {
+    constexpr int VW = 16 / int(sizeof(T));
+    auto by_nt = [&]<int VEC, int CPL>() -> int {
+        switch (ntmax) {
+            case 1:
+                if constexpr (rows_valid<T, VEC, CPL, 1>()) return f.template operator()<VEC, CPL, 1>();
+                break;
+            case 2:
+                if constexpr (rows_valid<T, VEC, CPL, 2>()) return f.template operator()<VEC, CPL, 2>();
+                break;
+            case 4:
+                if constexpr (rows_valid<T, VEC, CPL, 4>()) return f.template operator()<VEC, CPL, 4>();
+                break;
+            case 8:
+                if constexpr (rows_valid<T, VEC, CPL, 8>()) return f.template operator()<VEC, CPL, 8>();
+                break;
+        }
+        return GLMB_ERR_UNSUPPORTED;
+    };
+    auto by_cpl = [&]<int VEC>() -> int {
+        switch (cpl) {
+            case 1: return by_nt.template operator()<VEC, 1>();
+            case 2: return by_nt.template operator()<VEC, 2>();
+            case 4: return by_nt.template operator()<VEC, 4>();
+            case 8: return by_nt.template operator()<VEC, 8>();
+        }
+        return GLMB_ERR_UNSUPPORTED;
+    };
+    if (vec == VW) return by_cpl.template operator()<VW>();
+    if (vec == 1) return by_cpl.template operator()<1>();
+    return GLMB_ERR_UNSUPPORTED;
+}
+
+template <typename T, int VEC, int CPL, int NT>
+auto rows_kernel_for(int mode) {
+    if (mode == kRowsGrad) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGrad>;
+    if (mode == kRowsGradYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradYhat>;
+    return &glm_rows_kernel<T, VEC, CPL, NT, kRowsPredict>;
+}
+
+template <typename T, int VEC, int CPL, int NT>
+int rows_ctas_per_sm(int mode) {
+    // cached per instance and mode; every device this library runs on is a B200
+    static int cached[3] = {0, 0, 0};
+    int& c = cached[mode];
+    if (c == 0) {
+        using Shape = RowsShape<T, VEC, CPL, NT>;
+        const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;
+        auto kern = rows_kernel_for<T, VEC, CPL, NT>(mode);
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kRowsThreads, smem) != cudaSuccess)
+            n = 1;
+        c = std::max(1, n);
+    }
+    return c;
+}
+
+template <typename T>
+RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool vec_aligned,
+                   bool grad) {
+    RowsPlan p;
+    if (nf <= 0 || nt <= 0 || ntasks <= 0 || nobs < 0) return p;
+    constexpr int VW = 16 / int(sizeof(T));
+    p.vec = (vec_aligned && nf % VW == 0) ? VW : 1;
+    const int64_t nvec = nf / p.vec;
+    int cpl = 0;
+    for (int c : {1, 2, 4, 8})
+        if (int64_t(kWarp) * c >= nvec) {
+            cpl = c;
+            break;
+        }
+    if (cpl == 0) return p;
+    int ntmax = 0;
+    for (int n : {1, 2, 4, 8})
+        if (n >= nt) {
+            ntmax = n;
+            break;
+        }
+    if (ntmax == 0) return p;
+    if (ntmax * cpl * p.vec > rows_budget<T>()) return p;
+    p.cpl = cpl;
+    p.ntmax = ntmax;
+    const int64_t lanes = (nvec + cpl - 1) / cpl;
+    int seg_log2 = 0;
+    while ((int64_t(1) << seg_log2) < lanes) ++seg_log2;
+    p.seg_log2 = seg_log2;
+    const int mode = grad ? kRowsGrad : kRowsPredict;
+    int U = 1, per_sm = 1;
+    rows_dispatch<T>(p.vec, p.cpl, p.ntmax, [&]<int VEC, int CPL, int NT>() -> int {
+        U = RowsShape<T, VEC, CPL, NT>::U;
+        per_sm = rows_ctas_per_sm<T, VEC, CPL, NT>(mode);
+        return GLMB_OK;
+    });
+    const int64_t R = kWarp >> seg_log2;
+    const int64_t min_rows = int64_t(kRowsWarps) * U * R;
+    const int64_t target = int64_t(sm_count()) * per_sm;
+    int64_t cpt = std::max<int64_t>(1, (target + ntasks - 1) / ntasks);
+    cpt = std::min<int64_t>(cpt, std::max<int64_t>(1, (nobs + min_rows - 1) / min_rows));
+    int64_t opc = nobs > 0 ? (nobs + cpt - 1) / cpt : 1;
+    opc = (opc + R - 1) / R * R;
+    cpt = nobs > 0 ? (nobs + opc - 1) / opc : 0;
+    if (cpt * ntasks > int64_t(0x7fffffff)) return p;
+    p.ctas_per_task = int32_t(cpt);
+    p.obs_per_cta = opc;
+    p.part_doubles = size_t(ntasks) * size_t(nt) * size_t(nf) * size_t(cpt);
+    p.ok = true;
+    return p;
+}
+
+template <typename T>
+int rows_launch(const RowsPlan& p, int mode, const RowsArgs& args, cudaStream_t stream) {
+    if (p.ctas_per_task == 0) return GLMB_OK;
+    return rows_dispatch<T>(p.vec, p.cpl, p.ntmax, [&]<int VEC, int CPL, int NT>() -> int {
+        using Shape = RowsShape<T, VEC, CPL, NT>;
+        const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;
+        rows_ctas_per_sm<T, VEC, CPL, NT>(mode);  // sets the shared-memory attribute once
+        auto kern = rows_kernel_for<T, VEC, CPL, NT>(mode);
+        const dim3 grid(unsigned(int64_t(p.ctas_per_task) * args.ntasks));
+        kern<<<grid, kRowsThreads, smem, stream>>>(args);
+        count_launch();
+        return launch_status();
+    });
+}
+
+#define GLMB_INSTANTIATE_ROWS(T)                                                              \
+    template RowsPlan rows_plan<T>(int64_t, int64_t, int64_t, int64_t, bool, bool);          \
+    template int rows_launch<T>(const RowsPlan&, int, const RowsArgs&, cudaStream_t);
+
+}  // namespace glmb

@@ -1,0 +1,200 @@
+/*
+ * glm_b200.h -- C ABI of the B200 (sm_100a) GLM library, libglm_b200.so.
+ *
+ * Drop-in boundary for the GLM path of alexbaretta/gpu_algos.  In the
+ * reference, each kernel class launches its CUDA kernels from a member
+ * function `run_device_kernel(..., cudaStream_t)`; in this library the
+ * header-only kernel classes (gpu_algos_b200/include/cuda/kernels/glm/)
+ * make exactly one call into this ABI instead, and so can any C, C++,
+ * ctypes, cgo or JNI caller.
+ *
+ * Conventions shared by every entry point
+ *   - Plain C types only: device pointers, int64_t sizes, doubles, a stream.
+ *   - Memory layout is the reference's Tensor3D layout
+ *     (include/common/types/tensor3d.hpp:107-112 in the reference):
+ *       X     (nfeatures, ntasks, nobs)     X[(obs*ntasks + task)*nf + f]
+ *       Y     (ntargets,  ntasks, nobs)     Y[(obs*ntasks + task)*nt + t]
+ *       Yhat  same as Y
+ *       M     (nfeatures, ntargets, ntasks) M[(task*nt + t)*nf + f]
+ *       grad  same as M
+ *   - Launches are asynchronous on `stream` (NULL = legacy default stream);
+ *     no entry point synchronizes the device or the stream.
+ *   - Return value: 0 on success; a cudaError_t value (1..999) when a CUDA
+ *     call failed; a GLMB_ERR_* code (>= 1000) for invalid arguments.  No C++
+ *     exception crosses this boundary.
+ *   - Every output element is overwritten; outputs need no zeroing.
+ *   - Scratch memory ("workspace"): entry points that take `workspace` use
+ *     it when it is non-NULL and at least the size reported by the matching
+ *     *_workspace_size function; with workspace == NULL they obtain scratch
+ *     with cudaMallocAsync/cudaFreeAsync on `stream` (stream-ordered, no
+ *     synchronisation).
+ *   - Types: f16 (__half bits), f32, f64, i8, i16, i32, i64, u8, u16, u32,
+ *     u64 -- the eleven `--type` values of the reference mains
+ *     (src/cuda/benchmarks/glm/glm_gradient_xyyhat.cu:38-62).  Integer types
+ *     compute modulo 2^bits, as the reference's integer kernels do.
+ */
+#ifndef GLM_B200_H
+#define GLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* identical to cudaStream_t */
+typedef struct CUstream_st* glmb_stream_t;
+
+#define GLMB_OK 0
+#define GLMB_ERR_INVALID_VALUE 1001 /* negative size, NULL pointer for a non-empty tensor */
+#define GLMB_ERR_WORKSPACE 1002     /* workspace smaller than required */
+#define GLMB_ERR_UNSUPPORTED 1003   /* no device, or device is not sm_100 */
+#define GLMB_ERR_TOO_LARGE 1004     /* size beyond a documented limit */
+
+/* gradient flags */
+#define GLMB_GRAD_REGULARIZE 0x1u /* add lambda*(alpha*sign(M) + 2*(1-alpha)*M)   */
+#define GLMB_GRAD_WRITE_YHAT 0x2u /* also write Yhat = X.M (predictions)           */
+#define GLMB_GRAD_Y_ZERO 0x4u     /* Y is all zeros (Y may be NULL)               */
+
+/* Library version as an integer (major*10000 + minor*100 + patch). */
+int glmb_version(void);
+
+/* Human-readable text for a status code returned by any entry point. */
+const char* glmb_status_string(int status);
+
+/* Number of kernels this library has launched in this process. */
+uint64_t glmb_launch_count(void);
+
+/* Name of the kernel family the last gradient/predict call on this thread
+ * dispatched to ("rows", "generic", ...): diagnostics for tests. */
+const char* glmb_last_path(void);
+
+/* ------------------------------------------------------------------------
+ * Prediction: Yhat[t, task, obs] = sum_f M[f, t, task] * X[f, task, obs]
+ * Replaces Glm_predict_naive_kernel<T>::run_device_kernel
+ * (include/cuda/kernels/glm/glm_predict_naive.cuh:525-629).
+ * ---------------------------------------------------------------------- */
+#define GLMB_DECLARE_PREDICT(SFX, T)                                                    \
+    int glmb_predict_##SFX(const T* X, const T* M, T* Yhat, int64_t nfeatures,          \
+                           int64_t ntargets, int64_t ntasks, int64_t nobs,              \
+                           glmb_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Gradient of the squared-error loss, fused with the prediction:
+ *   grad[f,t,task] = 2 * sum_obs (Yhat - Y)[t,task,obs] * X[f,task,obs]
+ *                    [+ lambda*(alpha*sign(M) + 2*(1-alpha)*M)  if GLMB_GRAD_REGULARIZE]
+ * With GLMB_GRAD_REGULARIZE this replaces
+ *   Glm_gradient_xyyhat_kernel<T>::run_device_kernel
+ *   (include/cuda/kernels/glm/glm_gradient_xyyhat.cuh:642-783; the
+ *   prediction it stores in `temp` is written when GLMB_GRAD_WRITE_YHAT is set);
+ * without it this replaces
+ *   Glm_gradient_naive_kernel<T>::run_device_kernel
+ *   (include/cuda/kernels/glm/glm_gradient_naive.cuh:342-402).
+ * X is read from HBM once; yhat and the residual never leave the chip
+ * unless GLMB_GRAD_WRITE_YHAT asks for yhat.
+ * ---------------------------------------------------------------------- */
+#define GLMB_DECLARE_GRADIENT(SFX, T)                                                   \
+    size_t glmb_gradient_workspace_size_##SFX(int64_t nfeatures, int64_t ntargets,      \
+                                              int64_t ntasks, int64_t nobs);            \
+    int glmb_gradient_##SFX(const T* X, const T* M, const T* Y, T* grad_M, T* Yhat,     \
+                            int64_t nfeatures, int64_t ntargets, int64_t ntasks,        \
+                            int64_t nobs, double lambda, double alpha, uint32_t flags,  \
+                            void* workspace, size_t workspace_bytes,                    \
+                            glmb_stream_t stream);
+
+GLMB_DECLARE_PREDICT(f16, uint16_t)
+GLMB_DECLARE_PREDICT(f32, float)
+GLMB_DECLARE_PREDICT(f64, double)
+GLMB_DECLARE_PREDICT(i8, int8_t)
+GLMB_DECLARE_PREDICT(i16, int16_t)
+GLMB_DECLARE_PREDICT(i32, int32_t)
+GLMB_DECLARE_PREDICT(i64, int64_t)
+GLMB_DECLARE_PREDICT(u8, uint8_t)
+GLMB_DECLARE_PREDICT(u16, uint16_t)
+GLMB_DECLARE_PREDICT(u32, uint32_t)
+GLMB_DECLARE_PREDICT(u64, uint64_t)
+
+GLMB_DECLARE_GRADIENT(f16, uint16_t)
+GLMB_DECLARE_GRADIENT(f32, float)
+GLMB_DECLARE_GRADIENT(f64, double)
+GLMB_DECLARE_GRADIENT(i8, int8_t)
+GLMB_DECLARE_GRADIENT(i16, int16_t)
+GLMB_DECLARE_GRADIENT(i32, int32_t)
+GLMB_DECLARE_GRADIENT(i64, int64_t)
+GLMB_DECLARE_GRADIENT(u8, uint8_t)
+GLMB_DECLARE_GRADIENT(u16, uint16_t)
+GLMB_DECLARE_GRADIENT(u32, uint32_t)
+GLMB_DECLARE_GRADIENT(u64, uint64_t)
+
+/* ------------------------------------------------------------------------
+ * Sharded evaluation (observations split across GPUs).  The reference is
+ * single-GPU (no collective anywhere); these two calls split the gradient
+ * around the one exchange step a shard needs:
+ *   partial[f,t,task] = sum_{obs in shard} (Yhat - Y)[t,task,obs] * X[f,task,obs]
+ * in double, without the factor 2 and without the regularisation term; the
+ * caller sums the partials over shards (e.g. an NCCL all-reduce) and
+ * finalize applies  grad = 2*partial + lambda*(alpha*sign(M) + 2*(1-alpha)*M)
+ * exactly as glmb_gradient_* does on one GPU.
+ * ---------------------------------------------------------------------- */
+#define GLMB_DECLARE_SHARDED(SFX, T)                                                    \
+    int glmb_gradient_partial_##SFX(const T* X, const T* M, const T* Y, double* partial, \
+                                    T* Yhat, int64_t nfeatures, int64_t ntargets,       \
+                                    int64_t ntasks, int64_t nobs, uint32_t flags,       \
+                                    void* workspace, size_t workspace_bytes,            \
+                                    glmb_stream_t stream);                              \
+    int glmb_gradient_finalize_##SFX(const double* partial, const T* M, T* grad_M,      \
+                                     int64_t nfeatures, int64_t ntargets,               \
+                                     int64_t ntasks, double lambda, double alpha,       \
+                                     uint32_t flags, glmb_stream_t stream);
+
+GLMB_DECLARE_SHARDED(f32, float)
+GLMB_DECLARE_SHARDED(f64, double)
+
+/* ------------------------------------------------------------------------
+ * Elastic-net proximal gradient (ISTA).  No counterpart in the reference,
+ * which ships the gradient's elastic-net term
+ * (include/cuda/kernels/glm/glm_gradient_xyyhat.cuh:197-211) but no optimizer.
+ * Objective: sum (Yhat-Y)^2 + lambda1*|M|_1 + lambda2*|M|^2, i.e. the
+ * reference's regularised loss with lambda1 = lambda*alpha and
+ * lambda2 = lambda*(1-alpha).
+ * ---------------------------------------------------------------------- */
+#define GLMB_DECLARE_FIT(SFX, T)                                                        \
+    /* beta <- S(beta - grad_smooth*inv_L, l1*inv_L), S = soft threshold */             \
+    int glmb_prox_step_##SFX(T* beta, const T* grad_smooth, int64_t n, double inv_L,    \
+                             double l1, glmb_stream_t stream);                          \
+    /* One fused update from an (all-reduced) partial sum P of the smooth gradient: \
+     * g = 2P + 2*lambda2*beta;  beta <- S(beta - g/L[task], lambda1/L[task]),          \
+     * L read from device memory (one double per task). */                              \
+    int glmb_prox_update_##SFX(const double* partial, T* beta, const double* lipschitz, \
+                               int64_t nfeatures, int64_t ntargets, int64_t ntasks,     \
+                               double lambda1, double lambda2, glmb_stream_t stream);   \
+    /* Power-iteration step from an (all-reduced) partial P = X^T X v:                  \
+     * norm[task] = 2*|P_task|;  v_task <- P_task/|P_task|;  and                        \
+     * lipschitz[task] = safety*norm[task] + 2*lambda2 (safety = 1.05).                 \
+     * v, norm and lipschitz live in device memory. */                                  \
+    int glmb_power_step_##SFX(const double* partial, T* v, double* norm,                \
+                              double* lipschitz, int64_t nfeatures, int64_t ntasks,     \
+                              double lambda2, glmb_stream_t stream);                    \
+    /* Seeded start vector of the power iteration (SplitMix64, uniform [-1,1)),         \
+     * normalised per task, written to device memory v (nfeatures*ntasks). */            \
+    int glmb_power_init_##SFX(T* v, int64_t nfeatures, int64_t ntasks, uint64_t seed,   \
+                              glmb_stream_t stream);                                    \
+    /* Whole single-GPU fit: n_power power iterations for L, then n_iter ISTA steps     \
+     * from beta = 0.  lipschitz (device, ntasks doubles) receives L per task. */       \
+    size_t glmb_fit_workspace_size_##SFX(int64_t nfeatures, int64_t ntargets,           \
+                                         int64_t ntasks, int64_t nobs);                 \
+    int glmb_fit_elastic_net_##SFX(const T* X, const T* Y, T* beta, double* lipschitz,  \
+                                   int64_t nfeatures, int64_t ntargets, int64_t ntasks, \
+                                   int64_t nobs, double lambda1, double lambda2,        \
+                                   int n_power, int n_iter, uint64_t seed,              \
+                                   void* workspace, size_t workspace_bytes,             \
+                                   glmb_stream_t stream);
+
+GLMB_DECLARE_FIT(f32, float)
+GLMB_DECLARE_FIT(f64, double)
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GLM_B200_H */
