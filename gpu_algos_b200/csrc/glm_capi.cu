@@ -68,15 +68,6 @@ int check_device() {
 }
 
 template <typename T>
-struct Native {
-    using type = T;
-};
-template <>
-struct Native<uint16_t> {
-    using type = uint16_t;
-};
-
-template <typename T>
 constexpr bool kRowsType = std::is_same_v<T, float> || std::is_same_v<T, double>;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -99,7 +90,7 @@ int predict_impl(const T* X, const T* M, T* Yhat, int64_t nf, int64_t nt, int64_
         const RowsPlan p = rows_plan<T>(nf, nt, ntasks, nobs, aligned16(X), false);
         if (p.ok) {
             RowsArgs a{X, M, nullptr, Yhat, nullptr, nf, nt, ntasks, nobs, p.obs_per_cta,
-                       p.ctas_per_task, p.seg_log2};
+                       p.ctas_per_task, 0, p.ctas_per_task, p.seg_log2};
             set_last_path("rows");
             return rows_launch<T>(p, kRowsPredict, a, stream);
         }
@@ -158,7 +149,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
             Scratch sc(ws, ws_bytes, round_up(p.part_doubles * sizeof(double), 256), stream);
             if (sc.status() != GLMB_OK) return sc.status();
             RowsArgs a{X, M, Yin, Yhat_out, sc.as<double>(), nf, nt, ntasks, nobs, p.obs_per_cta,
-                       p.ctas_per_task, p.seg_log2};
+                       p.ctas_per_task, 0, p.ctas_per_task, p.seg_log2};
             set_last_path("rows");
             st = rows_launch<T>(p, write_yhat ? kRowsGradYhat : kRowsGrad, a, stream);
             if (st != GLMB_OK) return st;

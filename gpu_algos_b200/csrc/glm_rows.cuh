@@ -14,16 +14,15 @@
 // segment of S lanes (S a power of two <= 32); each lane owns CPL vectors of
 // VEC elements, feature f = (c*S + lane_in_segment)*VEC + v, so a warp load
 // instruction reads 32*VEC*sizeof(T) contiguous bytes (512 B for float4).
-// A warp handles 32/S rows per step and U steps per loop iteration, issuing
-// all U*CPL vector loads before the arithmetic that consumes them.  The dot
-// product is finished with an xor-butterfly inside the segment, which leaves
-// yhat in every lane of the segment.  Partial sums are carried in registers
-// in the input precision for kFlushSteps iterations, then folded across the
-// row groups of the warp and added into a per-warp double accumulator in
-// shared memory.  At the end the warps of a CTA are summed in a fixed order
-// and the CTA writes one double partial per (task, t, f); a second kernel
-// (glm_finalize.cuh) sums the CTA partials in a fixed order.  Results are
-// therefore deterministic for a given device and launch plan.
+// A warp handles 32/S rows per step and U steps per batch, issuing all
+// U*CPL vector loads of the next batch before the arithmetic of the current
+// one.  Partial sums are carried in registers in the input precision for
+// kFlushIters batches, then folded across the row groups of the warp and
+// added into a per-warp double accumulator in shared memory.  At the end the
+// warps of a CTA are summed in a fixed order and the CTA writes one double
+// partial per (task, t, f); glm_finalize_kernel (glm_generic.cu) sums the
+// CTA partials in a fixed order.  Results are therefore deterministic for a
+// given device and launch plan.
 #pragma once
 
 #include "glm_common.cuh"
@@ -41,12 +40,14 @@ struct RowsArgs {
     const void* M;
     const void* Y;  // may be NULL: all zeros
     void* Yhat;
-    double* part;  // [task][nt*nf][ctas_per_task]
+    double* part;  // [task][nt*nf][part_stride]
     int64_t nf;
     int64_t nt;
     int64_t ntasks;
     int64_t nobs;
     int64_t obs_per_cta;
+    int64_t part_stride;  // partials per (task, t, f): >= ctas_per_task
+    int64_t part_offset;  // column of this launch's first CTA
     int32_t ctas_per_task;
     int32_t seg_log2;
 };
@@ -55,16 +56,31 @@ template <typename T, int VEC, int CPL, int NT>
 struct RowsShape {
     static constexpr int FPL = CPL * VEC;  // features per lane
     static constexpr int WORDS = FPL * int(sizeof(T)) / 4 + NT;
-    static constexpr int U = (20 / WORDS) < 1 ? 1 : ((20 / WORDS) > 8 ? 8 : (20 / WORDS));
+    static constexpr int U_RAW = 20 / WORDS;
+    // rows (or row steps) per batch: a power of two in [1, 8]
+    static constexpr int U = U_RAW >= 8 ? 8 : (U_RAW >= 4 ? 4 : (U_RAW >= 2 ? 2 : 1));
+    static constexpr int LOG2U = U == 8 ? 3 : (U == 4 ? 2 : (U == 2 ? 1 : 0));
     static constexpr int SLOTS = NT * CPL * kWarp * VEC;  // doubles per warp in smem
     static constexpr size_t SMEM = size_t(kRowsWarps) * SLOTS * sizeof(double);
 };
 
-template <typename T, int VEC, int CPL, int NT, int MODE>
+// FULL: one row per warp (S = 32).  The U rows of a batch are then reduced
+// together: a transposed butterfly halves the set of rows a lane carries at
+// each of the first log2(U) exchange steps, so a batch of U rows costs
+// (U-1) + (5-log2 U) shuffles plus U broadcasts of the residual instead of
+// 5U shuffles; afterwards lane L holds the complete dot product of row
+// L >> (5 - log2 U).  Without FULL (S < 32, short rows) a warp carries 32/S
+// rows per step and each segment finishes its own butterfly.
+//
+// Loads are double-buffered in registers: the loads of batch i+1 are issued
+// before the arithmetic of batch i, so every warp keeps one batch of X in
+// flight while it computes.
+template <typename T, int VEC, int CPL, int NT, int MODE, bool FULL>
 __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a) {
     using D = typename Arith<T>::Dot;
     using Shape = RowsShape<T, VEC, CPL, NT>;
     constexpr int U = Shape::U;
+    constexpr int LOG2U = Shape::LOG2U;
     constexpr bool GRAD = MODE != kRowsPredict;
     extern __shared__ double smem_acc[];
 
@@ -75,9 +91,10 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 
     const int lane = threadIdx.x & (kWarp - 1);
     const int warp = threadIdx.x >> 5;
-    const int S = 1 << a.seg_log2;
-    const int R = kWarp >> a.seg_log2;  // rows per step
-    const int grp = lane >> a.seg_log2;
+    const int seg_log2 = FULL ? 5 : a.seg_log2;
+    const int S = 1 << seg_log2;
+    const int R = kWarp >> seg_log2;  // rows per step
+    const int grp = lane >> seg_log2;
     const int ls = lane & (S - 1);
     const int64_t task = blockIdx.x / a.ctas_per_task;
     const int64_t cta = blockIdx.x - task * a.ctas_per_task;
@@ -86,6 +103,8 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
     const int nt = static_cast<int>(a.nt);
     const int64_t nf = a.nf;
     const int64_t ntasks = a.ntasks;
+    // FULL: the batch row whose dot product this lane completes
+    const int u_mine = FULL ? (lane >> (5 - LOG2U)) : 0;
 
     // Model coefficients of this task, in registers.
     D m[NT][CPL][VEC];
@@ -121,73 +140,154 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                 for (int v = 0; v < VEC; ++v) {
                     D val = acc[t][c][v];
-                    for (int off = S; off < kWarp; off <<= 1)
-                        val += __shfl_xor_sync(0xffffffffu, val, off);
-                    if (grp == 0) wsm[((t * CPL + c) * kWarp + ls) * VEC + v] += double(val);
+                    if constexpr (!FULL) {
+                        for (int off = S; off < kWarp; off <<= 1)
+                            val += __shfl_xor_sync(0xffffffffu, val, off);
+                    }
+                    if (FULL || grp == 0) wsm[((t * CPL + c) * kWarp + ls) * VEC + v] += double(val);
                     acc[t][c][v] = D(0);
                 }
     };
 
-    const int64_t warp_stride = int64_t(kRowsWarps) * U * R;
-    int iters = 0;
-    for (int64_t base = obs_begin + int64_t(warp) * U * R; base < obs_end; base += warp_stride) {
-        T xv[U][CPL][VEC];
-        D yv[U][NT];
+    // Issue the loads of one batch: U steps of R rows starting at `base`.
+    // FULL batches load y only for the row whose residual this lane forms.
+    auto load = [&](T (&xb)[U][CPL][VEC], D (&yb)[U][NT], int64_t base) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t obs = base + int64_t(u) * R + grp;
             const bool ok = obs < obs_end;
-            const int64_t row = obs * ntasks + task;
-            const T* xrow = X + row * nf;
+            const T* xrow = X + (obs * ntasks + task) * nf;
 #pragma unroll
             for (int c = 0; c < CPL; ++c) {
                 const int64_t f0 = int64_t(c * S + ls) * VEC;
                 if (ok && f0 < nf) {
-                    VecLoad<T, VEC>::load(xrow + f0, xv[u][c]);
+                    VecLoad<T, VEC>::load(xrow + f0, xb[u][c]);
                 } else {
 #pragma unroll
-                    for (int v = 0; v < VEC; ++v) xv[u][c][v] = T(0);
+                    for (int v = 0; v < VEC; ++v) xb[u][c][v] = T(0);
                 }
-            }
-            if constexpr (GRAD) {
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    yv[u][t] = (ok && t < nt && Y != nullptr) ? to_arith<D>(Y[row * nt + t]) : D(0);
             }
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t obs = base + int64_t(u) * R + grp;
-            D r[NT];
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                D d = D(0);
-#pragma unroll
-                for (int c = 0; c < CPL; ++c)
-#pragma unroll
-                    for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], D(xv[u][c][v]), d);
-                for (int off = S >> 1; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-                if constexpr (MODE != kRowsGrad) {
-                    if (ls == 0 && t < nt && obs < obs_end) Yhat[(obs * ntasks + task) * nt + t] = T(d);
-                }
-                if constexpr (GRAD) r[t] = d - yv[u][t];
-            }
-            if constexpr (GRAD) {
+        if constexpr (GRAD) {
+            if constexpr (FULL) {
+                const int64_t obs = base + u_mine;
+                const bool ok = obs < obs_end && Y != nullptr;
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
+                    yb[0][t] = (ok && t < nt) ? to_arith<D>(Y[(obs * ntasks + task) * nt + t]) : D(0);
+            } else {
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t obs = base + int64_t(u) * R + grp;
+                    const bool ok = obs < obs_end && Y != nullptr;
+#pragma unroll
+                    for (int t = 0; t < NT; ++t)
+                        yb[u][t] = (ok && t < nt) ? to_arith<D>(Y[(obs * ntasks + task) * nt + t]) : D(0);
+                }
+            }
+        }
+    };
+
+    auto compute = [&](const T (&xb)[U][CPL][VEC], const D (&yb)[U][NT], int64_t base) {
+        if constexpr (FULL) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                D vals[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    D d = D(0);
 #pragma unroll
                     for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                        for (int v = 0; v < VEC; ++v)
-                            acc[t][c][v] = fma(r[t], D(xv[u][c][v]), acc[t][c][v]);
+                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], D(xb[u][c][v]), d);
+                    vals[u] = d;
+                }
+                // transposed butterfly over the first log2(U) lane bits
+#pragma unroll
+                for (int s = 0; s < LOG2U; ++s) {
+                    const int o = 16 >> s;
+                    const int half = U >> (s + 1);
+                    const bool hi = (lane & o) != 0;
+#pragma unroll
+                    for (int j = 0; j < half; ++j) {
+                        const D send = hi ? vals[j] : vals[j + half];
+                        const D keep = hi ? vals[j + half] : vals[j];
+                        vals[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                    }
+                }
+#pragma unroll
+                for (int o = 16 >> LOG2U; o > 0; o >>= 1) vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], o);
+                const D d = vals[0];  // dot product of row u_mine
+                if constexpr (MODE != kRowsGrad) {
+                    const int64_t obs = base + u_mine;
+                    if ((lane & ((32 >> LOG2U) - 1)) == 0 && t < nt && obs < obs_end)
+                        Yhat[(obs * ntasks + task) * nt + t] = T(d);
+                }
+                if constexpr (GRAD) {
+                    const D r_mine = d - yb[0][t];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const D r = __shfl_sync(0xffffffffu, r_mine, u << (5 - LOG2U));
+#pragma unroll
+                        for (int c = 0; c < CPL; ++c)
+#pragma unroll
+                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, D(xb[u][c][v]), acc[t][c][v]);
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t obs = base + int64_t(u) * R + grp;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    D d = D(0);
+#pragma unroll
+                    for (int c = 0; c < CPL; ++c)
+#pragma unroll
+                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], D(xb[u][c][v]), d);
+                    for (int off = S >> 1; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+                    if constexpr (MODE != kRowsGrad) {
+                        if (ls == 0 && t < nt && obs < obs_end) Yhat[(obs * ntasks + task) * nt + t] = T(d);
+                    }
+                    if constexpr (GRAD) {
+                        const D r = d - yb[u][t];
+#pragma unroll
+                        for (int c = 0; c < CPL; ++c)
+#pragma unroll
+                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, D(xb[u][c][v]), acc[t][c][v]);
+                    }
+                }
             }
         }
+    };
+
+    const int64_t warp_stride = int64_t(kRowsWarps) * U * R;
+    int iters = 0;
+    auto after_batch = [&]() {
         if constexpr (GRAD) {
             if (++iters == kFlushIters) {
                 flush();
                 iters = 0;
             }
         }
+    };
+    T xa[U][CPL][VEC], xb[U][CPL][VEC];
+    D ya[U][NT], yb[U][NT];
+    int64_t base = obs_begin + int64_t(warp) * U * R;
+    if (base < obs_end) load(xa, ya, base);
+    while (base < obs_end) {
+        int64_t next = base + warp_stride;
+        if (next < obs_end) load(xb, yb, next);
+        compute(xa, ya, base);
+        after_batch();
+        base = next;
+        if (base >= obs_end) break;
+        next = base + warp_stride;
+        if (next < obs_end) load(xa, ya, next);
+        compute(xb, yb, base);
+        after_batch();
+        base = next;
     }
     if constexpr (GRAD) {
         flush();
@@ -206,7 +306,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
             double s = 0.0;
 #pragma unroll
             for (int w = 0; w < kRowsWarps; ++w) s += smem_acc[size_t(w) * Shape::SLOTS + slot];
-            a.part[(task * K + int64_t(t) * nf + f) * a.ctas_per_task + cta] = s;
+            a.part[(task * K + int64_t(t) * nf + f) * a.part_stride + a.part_offset + cta] = s;
         }
     }
 }

@@ -55,14 +55,14 @@ int rows_dispatch(int vec, int cpl, int ntmax, F&& f) {
     return GLMB_ERR_UNSUPPORTED;
 }
 
-template <typename T, int VEC, int CPL, int NT>
+template <typename T, int VEC, int CPL, int NT, bool FULL>
 auto rows_kernel_for(int mode) {
-    if (mode == kRowsGrad) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGrad>;
-    if (mode == kRowsGradYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradYhat>;
-    return &glm_rows_kernel<T, VEC, CPL, NT, kRowsPredict>;
+    if (mode == kRowsGrad) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGrad, FULL>;
+    if (mode == kRowsGradYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradYhat, FULL>;
+    return &glm_rows_kernel<T, VEC, CPL, NT, kRowsPredict, FULL>;
 }
 
-template <typename T, int VEC, int CPL, int NT>
+template <typename T, int VEC, int CPL, int NT, bool FULL>
 int rows_ctas_per_sm(int mode) {
     // cached per instance and mode; every device this library runs on is a B200
     static int cached[3] = {0, 0, 0};
@@ -70,7 +70,7 @@ int rows_ctas_per_sm(int mode) {
     if (c == 0) {
         using Shape = RowsShape<T, VEC, CPL, NT>;
         const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;
-        auto kern = rows_kernel_for<T, VEC, CPL, NT>(mode);
+        auto kern = rows_kernel_for<T, VEC, CPL, NT, FULL>(mode);
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         int n = 0;
@@ -114,7 +114,11 @@ RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool ve
     int U = 1, per_sm = 1;
     rows_dispatch<T>(p.vec, p.cpl, p.ntmax, [&]<int VEC, int CPL, int NT>() -> int {
         U = RowsShape<T, VEC, CPL, NT>::U;
-        per_sm = rows_ctas_per_sm<T, VEC, CPL, NT>(mode);
+        if (seg_log2 == 5) {
+            per_sm = rows_ctas_per_sm<T, VEC, CPL, NT, true>(mode);
+        } else if constexpr (CPL == 1) {
+            per_sm = rows_ctas_per_sm<T, VEC, CPL, NT, false>(mode);
+        }
         return GLMB_OK;
     });
     const int64_t R = kWarp >> seg_log2;
@@ -139,10 +143,18 @@ int rows_launch(const RowsPlan& p, int mode, const RowsArgs& args, cudaStream_t 
     return rows_dispatch<T>(p.vec, p.cpl, p.ntmax, [&]<int VEC, int CPL, int NT>() -> int {
         using Shape = RowsShape<T, VEC, CPL, NT>;
         const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;
-        rows_ctas_per_sm<T, VEC, CPL, NT>(mode);  // sets the shared-memory attribute once
-        auto kern = rows_kernel_for<T, VEC, CPL, NT>(mode);
         const dim3 grid(unsigned(int64_t(p.ctas_per_task) * args.ntasks));
-        kern<<<grid, kRowsThreads, smem, stream>>>(args);
+        if (p.seg_log2 == 5) {
+            rows_ctas_per_sm<T, VEC, CPL, NT, true>(mode);  // sets the shared-memory attribute once
+            rows_kernel_for<T, VEC, CPL, NT, true>(mode)<<<grid, kRowsThreads, smem, stream>>>(args);
+        } else {
+            if constexpr (CPL == 1) {
+                rows_ctas_per_sm<T, VEC, CPL, NT, false>(mode);
+                rows_kernel_for<T, VEC, CPL, NT, false>(mode)<<<grid, kRowsThreads, smem, stream>>>(args);
+            } else {
+                return GLMB_ERR_UNSUPPORTED;  // CPL > 1 always spans a full warp
+            }
+        }
         count_launch();
         return launch_status();
     });
