@@ -80,6 +80,8 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"glmb_fit_workspace_size_{s}")
         f.argtypes = [_I64, _I64, _I64, _I64]
         f.restype = _SZ
+    L.glmb_gradient_noalloc_f32.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P]
+    L.glmb_gradient_noalloc_f32.restype = _INT
 
 
 def lib() -> ctypes.CDLL:
@@ -132,4 +134,5 @@ def exported_symbols() -> list[str]:
         names += [f"glmb_gradient_partial_{s}", f"glmb_gradient_finalize_{s}", f"glmb_prox_step_{s}",
                   f"glmb_prox_update_{s}", f"glmb_power_step_{s}", f"glmb_power_init_{s}",
                   f"glmb_fit_workspace_size_{s}", f"glmb_fit_elastic_net_{s}"]
+    names.append("glmb_gradient_noalloc_f32")
     return names

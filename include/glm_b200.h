@@ -128,6 +128,25 @@ GLMB_DECLARE_GRADIENT(u32, uint32_t)
 GLMB_DECLARE_GRADIENT(u64, uint64_t)
 
 /* ------------------------------------------------------------------------
+ * Gradient that allocates no device memory (float32).  No counterpart in
+ * the reference: it exists for callers that may not allocate -- a host that
+ * owns every device buffer and passes a plugin only its inputs and outputs,
+ * a fixed device-memory budget, a path that must not wait on the allocator.
+ * Same arguments and result as glmb_gradient_f32, minus the workspace: the
+ * scratch is a 4 MiB array inside the library, resident on every GPU that
+ * loads it until the process exits.  Limits: nfeatures*ntargets*ntasks <=
+ * 524288 (else GLMB_ERR_TOO_LARGE), ntargets <= 8 and nfeatures <= 1024
+ * (else GLMB_ERR_UNSUPPORTED).  All calls on a device share the array:
+ * calls whose kernels overlap on the GPU race, so order them (one stream or
+ * events).  The first call on each device looks up the array's address;
+ * make it before any stream capture begins.
+ * ---------------------------------------------------------------------- */
+int glmb_gradient_noalloc_f32(const float* X, const float* M, const float* Y, float* grad_M,
+                              float* Yhat, int64_t nfeatures, int64_t ntargets, int64_t ntasks,
+                              int64_t nobs, double lambda, double alpha, uint32_t flags,
+                              glmb_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Sharded evaluation (observations split across GPUs).  The reference is
  * single-GPU (no collective anywhere); these two calls split the gradient
  * around the one exchange step a shard needs:
