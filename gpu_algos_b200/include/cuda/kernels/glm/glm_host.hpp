@@ -2,10 +2,13 @@
 // run_host_kernel, and the typed bridge from the kernel classes to the C ABI.
 //
 // run_host_kernel is the reference API's CPU implementation (the driver
-// compares the GPU result with it).  The arithmetic follows the reference's
-// Number type: float/double in their own precision, integers modulo 2^bits
-// (carried in the unsigned type of the same or 32-bit width, so wrapping is
-// defined), half in float rounded on store.
+// compares the GPU result with it).  Results are rounded to the Number type
+// as the reference's are; sums are carried wider than the reference's own
+// Eigen product so that the driver's check (relative error <= 2^-20 for
+// float) measures the GPU's rounding rather than the host's: float in
+// double, double in long double, half in float.  Integers compute modulo
+// 2^bits (in the unsigned type of 32 or 64 bits, so wrapping is defined),
+// bit-identical to the reference.
 #pragma once
 
 #include <algorithm>
@@ -26,8 +29,9 @@ template <typename T>
 struct Arith {
     using type = std::conditional_t<
         std::is_same_v<T, __half>, float,
-        std::conditional_t<std::is_integral_v<T>,
-                           std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>, T>>;
+        std::conditional_t<std::is_same_v<T, float>, double,
+                           std::conditional_t<std::is_same_v<T, double>, long double,
+                                              std::conditional_t<(sizeof(T) <= 4), uint32_t, uint64_t>>>>;
 };
 template <typename T>
 using arith_t = typename Arith<T>::type;
