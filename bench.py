@@ -275,6 +275,10 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     lam = args.lam
 
+    from gpu_algos_b200.sharded import CudaBackend, ShardedGLM
+
+    backend = CudaBackend(workspace=ws)
+
     def step(ev=None):
         if ev is not None:
             ev[0].record(stream)
@@ -283,11 +287,11 @@ def run_ours(args):
             if ev is not None:
                 ev[1].record(stream)
         else:
-            glm.gradient_partial(X, beta, Y, out=partial, workspace=ws)
+            backend.partial(X, beta, Y, out=partial)
             if ev is not None:
                 ev[1].record(stream)
             dist.all_reduce(partial, op=dist.ReduceOp.SUM)
-            glm.gradient_finalize(partial, beta, lam, 0.0, True, out=grad)
+            backend.finalize(partial, beta, lam, 0.0, grad)
 
     props = torch.cuda.get_device_properties(device)
     sampler = ClockSampler(f"GPU-{props.uuid}")
@@ -341,9 +345,7 @@ def run_ours(args):
             if world == 1:
                 glm.gradient(Xd, beta, Yd, lam, 0.0, True, out=grad, workspace=ws)
             else:
-                glm.gradient_partial(Xd, beta, Yd, out=partial, workspace=ws)
-                dist.all_reduce(partial, op=dist.ReduceOp.SUM)
-                glm.gradient_finalize(partial, beta, lam, 0.0, True, out=grad)
+                ShardedGLM(Xd, Yd, backend).gradient(beta, lam, 0.0, out=grad)
             gh.copy_(grad, non_blocking=True)
 
         e2e_step()

@@ -1,0 +1,153 @@
+"""Observation-sharded GLM gradient and elastic-net fit across ranks.
+
+The reference is single-GPU.  Here the observations are split into
+contiguous blocks, one per rank (one process per GPU, ``torch.distributed``
+for the plumbing): every rank evaluates
+
+    P_r = sum_{obs in block r} (Yhat - Y) X          (float64, no factor 2)
+
+with the fused kernel (``glmb_gradient_partial_*``), the P_r are summed with
+ONE all-reduce, and every rank applies the same finalize step, so all ranks
+hold bit-identical gradients / coefficients.  Tasks shard with no collective
+at all (each task's gradient only involves its own observations), which is
+what :func:`task_range` is for.
+
+The per-rank arithmetic goes through a :class:`Backend`: :class:`CudaBackend`
+calls ``libglm_b200.so``; the CPU tests supply their own backend and run the
+same orchestration on ``gloo`` ranks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+#: safety factor applied to the power-iteration estimate of the Lipschitz constant
+POWER_SAFETY = 1.05
+
+
+def obs_range(nobs: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous block [lo, hi) of observations owned by ``rank``; the
+    first ``nobs % world`` ranks hold one extra observation."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, extra = divmod(nobs, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def task_range(ntasks: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous block [lo, hi) of tasks owned by ``rank`` (task sharding)."""
+    return obs_range(ntasks, world, rank)
+
+
+class Backend:
+    """Per-rank arithmetic of the sharded path (all tensors on one device)."""
+
+    def partial(self, X, M, Y):  # -> float64 (ntasks, nt, nf)
+        raise NotImplementedError
+
+    def finalize(self, P, M, lam, alpha, out):  # grad = 2P + elastic-net term
+        raise NotImplementedError
+
+    def power_init(self, v, seed):
+        raise NotImplementedError
+
+    def power_step(self, P, v, norm, lipschitz, lambda2):
+        raise NotImplementedError
+
+    def prox_update(self, P, beta, lipschitz, lambda1, lambda2):
+        raise NotImplementedError
+
+
+class CudaBackend(Backend):
+    """The sm_100a kernels of libglm_b200.so."""
+
+    def __init__(self, workspace=None):
+        from . import glm
+
+        self.glm = glm
+        self.workspace = workspace
+
+    def partial(self, X, M, Y, out=None):
+        return self.glm.gradient_partial(X, M, Y, out=out, workspace=self.workspace)
+
+    def finalize(self, P, M, lam, alpha, out):
+        return self.glm.gradient_finalize(P, M, lam, alpha, True, out=out)
+
+    def power_init(self, v, seed):
+        return self.glm.power_init(v, seed)
+
+    def power_step(self, P, v, norm, lipschitz, lambda2):
+        return self.glm.power_step(P, v, norm, lipschitz, lambda2)
+
+    def prox_update(self, P, beta, lipschitz, lambda1, lambda2):
+        return self.glm.prox_update(P, beta, lipschitz, lambda1, lambda2)
+
+
+def _all_reduce(t, group):
+    if group is not None or (dist.is_available() and dist.is_initialized()):
+        if dist.get_world_size(group) > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return t
+
+
+@dataclass
+class ShardedGLM:
+    """This rank's block of observations and the collective that joins them.
+
+    X_local: (nobs_local, ntasks, nf), Y_local: (nobs_local, ntasks, nt).
+    Every rank must make the same sequence of calls (they all take part in
+    each all-reduce).
+    """
+
+    X_local: torch.Tensor
+    Y_local: torch.Tensor
+    backend: Backend
+    group: object = None
+
+    def partial_sum(self, M, Y=None, y_zero=False):
+        P = self.backend.partial(self.X_local, M, None if y_zero else (self.Y_local if Y is None else Y))
+        return _all_reduce(P, self.group)
+
+    def gradient(self, M, lam: float, alpha: float, out=None):
+        """Full-data gradient 2 sum (Yhat - Y) X + lam(alpha sign M + 2(1-alpha) M)."""
+        P = self.partial_sum(M)
+        if out is None:
+            out = torch.empty_like(M)
+        return self.backend.finalize(P, M, lam, alpha, out)
+
+    def fit_elastic_net(self, lambda1: float, lambda2: float, n_power: int = 20, n_iter: int = 200,
+                        seed: int = 42, checkpoint=None, resume=None):
+        """ISTA on the sharded data: returns (beta, lipschitz per task).
+
+        ``checkpoint(it, beta, lipschitz)`` (optional) is called after every
+        iteration on every rank; ``resume=(it, beta, lipschitz)`` restarts
+        from a snapshot taken that way (skipping the power iteration).
+        """
+        ntasks, nf = self.X_local.shape[1], self.X_local.shape[2]
+        nt = self.Y_local.shape[2]
+        dev, dt = self.X_local.device, self.X_local.dtype
+        if resume is not None:
+            start, beta0, lip0 = resume
+            beta = beta0.clone().to(dev)
+            lipschitz = lip0.clone().to(dev)
+        else:
+            start = 0
+            v = torch.empty((ntasks, 1, nf), dtype=dt, device=dev)
+            norm = torch.empty((ntasks,), dtype=torch.float64, device=dev)
+            lipschitz = torch.empty((ntasks,), dtype=torch.float64, device=dev)
+            self.backend.power_init(v, seed)
+            for _ in range(n_power):
+                P = self.backend.partial(self.X_local, v, None)
+                _all_reduce(P, self.group)
+                self.backend.power_step(P, v, norm, lipschitz, lambda2)
+            beta = torch.zeros((ntasks, nt, nf), dtype=dt, device=dev)
+        for it in range(start, n_iter):
+            P = self.backend.partial(self.X_local, beta, self.Y_local)
+            _all_reduce(P, self.group)
+            self.backend.prox_update(P, beta, lipschitz, lambda1, lambda2)
+            if checkpoint is not None:
+                checkpoint(it + 1, beta, lipschitz)
+        return beta, lipschitz

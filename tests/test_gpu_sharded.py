@@ -1,0 +1,85 @@
+"""Observation-sharded gradient and fit across 2 GPUs (NCCL), one process
+per GPU, checked against the single-GPU entry points on the full data.
+Skipped when fewer than two GPUs are visible."""
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:  # pragma: no cover
+    pytest.skip("needs two CUDA devices", allow_module_level=True)
+
+import torch.multiprocessing as mp  # noqa: E402
+
+
+def _problem(dt):
+    rng = np.random.default_rng(8)
+    nobs, ntasks, nf, nt = 200_003, 2, 96, 2
+    X = rng.uniform(-1, 1, (nobs, ntasks, nf)).astype(dt)
+    bt = rng.normal(size=(ntasks, nt, nf)) * (rng.uniform(size=(ntasks, nt, nf)) < 0.3)
+    Y = (np.einsum("otf,tkf->otk", X.astype(np.float64), bt) + 0.1 * rng.normal(size=(nobs, ntasks, nt))).astype(dt)
+    M = rng.uniform(0, 1, (ntasks, nt, nf)).astype(dt)
+    return X, Y, M
+
+
+def _worker(rank, world, port, outdir, dt_name):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from gpu_algos_b200.sharded import CudaBackend, ShardedGLM, obs_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        X, Y, M = _problem(np.dtype(dt_name))
+        lo, hi = obs_range(X.shape[0], world, rank)
+        sh = ShardedGLM(torch.from_numpy(X[lo:hi].copy()).cuda(), torch.from_numpy(Y[lo:hi].copy()).cuda(),
+                        CudaBackend())
+        g = sh.gradient(torch.from_numpy(M).cuda(), 0.2, 0.3)
+        beta, lip = sh.fit_elastic_net(50.0, 5.0, n_power=20, n_iter=40, seed=11)
+        torch.cuda.synchronize()
+        np.save(os.path.join(outdir, f"g{rank}.npy"), g.cpu().numpy())
+        np.save(os.path.join(outdir, f"b{rank}.npy"), beta.cpu().numpy())
+        np.save(os.path.join(outdir, f"l{rank}.npy"), lip.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_two_gpu_sharded_matches_single_gpu(dt):
+    outdir = tempfile.mkdtemp()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, outdir, np.dtype(dt).name)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert not p.is_alive(), "a rank hung"
+        assert p.exitcode == 0
+    from gpu_algos_b200 import glm
+
+    X, Y, M = _problem(dt)
+    tX, tY, tM = (torch.from_numpy(a).cuda() for a in (X, Y, M))
+    g_ref = glm.gradient(tX, tM, tY, 0.2, 0.3).cpu().numpy()
+    b_ref, l_ref = glm.fit_elastic_net(tX, tY, 50.0, 5.0, n_power=20, n_iter=40, seed=11)
+    b_ref, l_ref = b_ref.cpu().numpy(), l_ref.cpu().numpy()
+    g0, g1 = np.load(os.path.join(outdir, "g0.npy")), np.load(os.path.join(outdir, "g1.npy"))
+    assert np.array_equal(g0, g1)
+    tol = 1e-4 if dt == np.float32 else 1e-11
+    assert np.max(np.abs(g0 - g_ref) / np.abs(g_ref)) <= tol
+    b0 = np.load(os.path.join(outdir, "b0.npy"))
+    assert np.array_equal(b0, np.load(os.path.join(outdir, "b1.npy")))
+    assert np.allclose(np.load(os.path.join(outdir, "l0.npy")), l_ref, rtol=tol)
+    assert np.max(np.abs(b0 - b_ref)) <= (1e-3 if dt == np.float32 else 1e-9) * np.max(np.abs(b_ref))
