@@ -1,17 +1,27 @@
 #!/usr/bin/env python
-"""Benchmark of the fused GLM gradient on B200 (one process per GPU).
+"""Benchmark of the GLM path on B200 (one process per GPU).
 
-Workload (default): one full gradient evaluation of the memory-bound
-single-task GLM -- nobs = 2^24 observations, nfeatures = 128, ntargets = 1,
-ntasks = 1, float32, X ~ U(-1, 1), beta ~ N(0, 1), y = X beta + N(0, 0.1^2),
-lambda2 = 0.01 (lambda = 0.01, alpha = 0).  X is 8 GiB, far larger than L2
-(126 MB), so no flush is needed between steps.  Observations are split
-into contiguous blocks, one per rank (strong scaling: the total is fixed);
-each rank computes its partial sum, the partials are summed with one NCCL
-all-reduce, and every rank applies 2*sum + the elastic-net term.
+Default workload ("gradient"): one full gradient evaluation of the
+memory-bound single-task GLM -- nobs = 2^24 observations, nfeatures = 128,
+ntargets = 1, ntasks = 1, float32, X ~ U(-1, 1), beta ~ N(0, 1),
+y = X beta + N(0, 0.1^2), lambda2 = 0.01 (lambda = 0.01, alpha = 0).  X is
+8 GiB, far larger than L2 (126 MB), so no flush is needed between steps.
+Observations are split into contiguous blocks, one per rank (strong scaling:
+the total is fixed); each rank computes its partial sum, the partials are
+summed with one NCCL all-reduce, and every rank applies 2*sum + the
+elastic-net term.
+
+Other workloads (--workload):
+  driver     nobs 8192, nfeatures 32, float32: the reference driver's
+             CPU-checkable shape (too small to shard: replicas per GPU)
+  multitask  64 tasks x 2^18 observations x 256 features x 16 targets,
+             float64 (tasks sharded across ranks, no collective)
+  fit        elastic-net fit, 20 power iterations + 200 ISTA steps,
+             nobs 2^26, nfeatures 512, float32, lambda1 0.05, lambda2 0.01,
+             10 %-sparse true coefficients (observations sharded)
 
 Usage:
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Rank 0 prints one JSON line.  `--impl reference` times the reference's CPU
@@ -28,6 +38,7 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
@@ -36,40 +47,97 @@ if REPO not in sys.path:
 METRIC = "GLM gradient obs·features/s"
 UNIT = "obs·features/s"
 FALLBACK_HBM_GBS = 6650.0
+HOST_PIN_LIMIT = 40 << 30  # largest per-rank X copied through pinned host memory for e2e
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    nobs: int
+    nf: int
+    nt: int
+    ntasks: int
+    dtype: str  # "f32" | "f64"
+    x: str  # "uniform" (U(-1,1)) | "normal" (N(0,1))
+    noise: float
+    shard: str  # "obs" | "tasks" | "replica"
+    kind: str = "gradient"  # "gradient" | "fit"
+    lam: float = 0.0
+    alpha: float = 0.0
+    independent_beta: bool = False  # gradient at a model other than the true one
+    sparsity: float = 1.0  # fraction of non-zero true coefficients
+    lambda1: float = 0.0
+    lambda2: float = 0.0
+    n_power: int = 0
+    n_iter: int = 0
+    block: int = 1 << 16  # rows per seeded generation block
+
+
+WORKLOADS = {
+    "gradient": Workload("gradient", 1 << 24, 128, 1, 1, "f32", "uniform", 0.1, "obs", lam=0.01),
+    "driver": Workload("driver", 8192, 32, 1, 1, "f32", "uniform", 0.01, "replica", lam=0.1,
+                       independent_beta=True, block=8192),
+    "multitask": Workload("multitask", 1 << 18, 256, 16, 64, "f64", "normal", 0.05, "tasks", lam=0.1,
+                          independent_beta=True, block=1 << 14),
+    "fit": Workload("fit", 1 << 26, 512, 1, 1, "f32", "normal", 0.1, "obs", kind="fit", sparsity=0.1,
+                    lambda1=0.05, lambda2=0.01, n_power=20, n_iter=200),
+}
 
 
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=500)
-    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--steps", type=int, default=None, help="timed steps (default: per workload)")
+    p.add_argument("--warmup", type=int, default=None)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--nobs", type=int, default=1 << 24)
-    p.add_argument("--nfeatures", type=int, default=128)
-    p.add_argument("--lam", type=float, default=0.01)
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="gradient")
+    p.add_argument("--nobs", type=int, default=None, help="override the workload's nobs")
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
+    a = p.parse_args()
+    w = WORKLOADS[a.workload]
+    if a.nobs is not None:
+        w = Workload(**{**w.__dict__, "nobs": a.nobs, "block": min(w.block, a.nobs)})
+    a.w = w
+    default_steps = {"gradient": 500, "driver": 2000, "multitask": 20, "fit": 2}[w.name]
+    a.steps = a.steps if a.steps is not None else default_steps
+    a.warmup = a.warmup if a.warmup is not None else (1 if w.kind == "fit" else 10)
+    return a
 
 
-def workload_config(args, n_gpus):
-    return {
-        "workload": f"glm_gradient f32 nobs={args.nobs} nfeatures={args.nfeatures} ntargets=1 ntasks=1",
-        "nobs": args.nobs,
-        "nfeatures": args.nfeatures,
-        "ntargets": 1,
-        "ntasks": 1,
-        "lambda": args.lam,
-        "alpha": 0.0,
-        "inputs": "X~U(-1,1), beta~N(0,1), y=X beta+N(0,0.1^2), seeded",
-        "l2": "inputs larger than L2 (X 8 GiB), no flush",
-        "parallelism": f"obs-sharded x{n_gpus} + NCCL all-reduce of the partial gradient" if n_gpus > 1 else "single GPU",
+def passes_per_step(w: Workload) -> int:
+    return (w.n_power + w.n_iter) if w.kind == "fit" else 1
+
+
+def workload_config(w: Workload, n_gpus: int) -> dict:
+    cfg = {
+        "workload": (f"glm_{'fit_elastic_net' if w.kind == 'fit' else 'gradient'} {w.dtype} nobs={w.nobs} "
+                     f"nfeatures={w.nf} ntargets={w.nt} ntasks={w.ntasks}"),
+        "nobs": w.nobs, "nfeatures": w.nf, "ntargets": w.nt, "ntasks": w.ntasks,
+        "inputs": (f"X~{'U(-1,1)' if w.x == 'uniform' else 'N(0,1)'}, beta~N(0,1)"
+                   + (f" {int(w.sparsity * 100)}%-sparse" if w.sparsity < 1 else "")
+                   + f", y=X beta+N(0,{w.noise}^2), seeded"),
+        "l2": "inputs larger than L2 (126 MB), no flush" if w.nobs * w.ntasks * w.nf * 4 > (256 << 20)
+              else "inputs smaller than L2 (launch-bound shape)",
     }
+    if w.kind == "fit":
+        cfg.update(lambda1=w.lambda1, lambda2=w.lambda2, n_power=w.n_power, n_iter=w.n_iter)
+    else:
+        cfg.update({"lambda": w.lam, "alpha": w.alpha})
+    if n_gpus == 1:
+        cfg["parallelism"] = "single GPU"
+    elif w.shard == "obs":
+        cfg["parallelism"] = f"obs-sharded x{n_gpus} + one NCCL all-reduce of the partial gradient per pass"
+    elif w.shard == "tasks":
+        cfg["parallelism"] = f"tasks-sharded x{n_gpus}, no collective"
+    else:
+        cfg["parallelism"] = f"{n_gpus} independent replicas (shape too small to shard)"
+    return cfg
 
 
-def algorithmic_bytes(nobs, nf, nt=1, ntasks=1, esize=4):
+def algorithmic_bytes(nobs, nf, nt, ntasks, esize):
     """X once, Y once, M in and grad out."""
     return esize * (nobs * ntasks * nf + nobs * ntasks * nt + 2 * nf * nt * ntasks)
 
@@ -83,12 +151,14 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def dram_traffic_per_row():
-    """DRAM bytes per observation row of the rows kernel from the committed
-    ncu summary (profiles/glm_rows_f32_nf128_traffic.txt), or None."""
-    path = os.path.join(REPO, "profiles", "glm_rows_f32_nf128_traffic.txt")
+def dram_traffic_per_row(w: Workload):
+    """DRAM bytes per observation row of the dominant kernel, from the
+    committed ncu summary of that kernel and shape, or None."""
+    name = {"gradient": "glm_rows_f32_nf128_traffic.txt"}.get(w.name)
+    if name is None:
+        return None
     try:
-        with open(path) as f:
+        with open(os.path.join(REPO, "profiles", name)) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_row:"):
                     return float(line.split(":", 1)[1])
@@ -97,68 +167,88 @@ def dram_traffic_per_row():
     return None
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 # --------------------------------------------------------------------------
-# reference arm: the reference's CPU algorithm on the host cores
+# CPU: the reference's algorithm (oracle port) on the host cores
 # --------------------------------------------------------------------------
-def cpu_sample_rate(nf, rows, lam, reps=3, threads=0):
-    """obs·features/s of the oracle's gradient (the reference's host
-    algorithm) on `rows` observations; best of `reps`."""
+def cpu_problem(w: Workload, rows: int):
     import numpy as np
 
+    rng = np.random.default_rng(7)
+    dt = np.float32 if w.dtype == "f32" else np.float64
+    if w.x == "uniform":
+        X = rng.uniform(-1, 1, (rows, w.ntasks, w.nf)).astype(dt)
+    else:
+        X = rng.normal(size=(rows, w.ntasks, w.nf)).astype(dt)
+    b = rng.normal(size=(w.ntasks, w.nt, w.nf)).astype(dt)
+    Y = (np.einsum("otf,tkf->otk", X, b) + w.noise * rng.normal(size=(rows, w.ntasks, w.nt))).astype(dt)
+    return X, b, Y
+
+
+def cpu_pass(pyoracle, w: Workload, X, b, Y):
+    if w.kind == "fit":
+        return pyoracle.gradient(X, b, Y, w.lambda2, 0.0, True)
+    return pyoracle.gradient(X, b, Y, w.lam, w.alpha, True)
+
+
+def cpu_sample_rate(w: Workload, rows: int, reps: int = 3):
+    """obs·features/s of one oracle pass (the reference's host algorithm)
+    over `rows` observations on all host threads; best of `reps`."""
     from oracle import pyoracle
 
     pyoracle.build()
-    if threads:
-        pyoracle.set_threads(threads)
-    rng = np.random.default_rng(7)
-    X = rng.uniform(-1, 1, (rows, 1, nf)).astype(np.float32)
-    b = rng.normal(size=(1, 1, nf)).astype(np.float32)
-    Y = (X[:, 0, :] @ b[0, 0] + rng.normal(0, 0.1, rows)).astype(np.float32).reshape(rows, 1, 1)
+    pyoracle.set_threads(host_threads())
+    X, b, Y = cpu_problem(w, rows)
     best = float("inf")
     for _ in range(reps):
         t0 = time.perf_counter()
-        pyoracle.gradient(X, b, Y, lam, 0.0, True)
+        cpu_pass(pyoracle, w, X, b, Y)
         best = min(best, time.perf_counter() - t0)
-    return rows * nf / best, pyoracle.get_threads(), best
+    return rows * w.ntasks * w.nf / best, pyoracle.get_threads(), best
+
+
+def cpu_rows(w: Workload) -> int:
+    return min(w.nobs, {"gradient": 1 << 21, "driver": 8192, "multitask": 4096, "fit": 1 << 19}[w.name])
 
 
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    w = args.w
+    if int(os.environ.get("RANK", "0")) != 0:
         return 0
     from oracle import pyoracle
 
     pyoracle.build()
-    import numpy as np
-
-    nf = args.nfeatures
-    # size each step's sample so the whole run stays near a minute of CPU time
-    probe_rows = min(args.nobs, 1 << 21)
-    rng = np.random.default_rng(7)
-    X = rng.uniform(-1, 1, (probe_rows, 1, nf)).astype(np.float32)
-    b = rng.normal(size=(1, 1, nf)).astype(np.float32)
-    Y = (X[:, 0, :] @ b[0, 0] + rng.normal(0, 0.1, probe_rows)).astype(np.float32).reshape(probe_rows, 1, 1)
-    pyoracle.gradient(X, b, Y, args.lam, 0.0, True)
+    pyoracle.set_threads(host_threads())
+    rows = cpu_rows(w)
+    X, b, Y = cpu_problem(w, rows)
+    cpu_pass(pyoracle, w, X, b, Y)
     t0 = time.perf_counter()
-    pyoracle.gradient(X, b, Y, args.lam, 0.0, True)
+    cpu_pass(pyoracle, w, X, b, Y)
     t1 = time.perf_counter() - t0
+    # each step is a bounded sample: keep the whole run near a minute of CPU time
     budget = 60.0 / max(1, args.steps + args.warmup)
-    rows = int(probe_rows * min(1.0, budget / max(t1, 1e-9)))
-    rows = max(1 << 12, min(probe_rows, rows))
+    rows = max(min(rows, 64), int(rows * min(1.0, budget / max(t1, 1e-9))))
     X, Y = X[:rows], Y[:rows]
     for _ in range(args.warmup):
-        pyoracle.gradient(X, b, Y, args.lam, 0.0, True)
+        cpu_pass(pyoracle, w, X, b, Y)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        pyoracle.gradient(X, b, Y, args.lam, 0.0, True)
+        cpu_pass(pyoracle, w, X, b, Y)
     dt = time.perf_counter() - t0
-    value = rows * nf * args.steps / dt
-    sample = f"{rows} of {args.nobs} observations per step (nfeatures={nf}), float32"
+    value = rows * w.ntasks * w.nf * args.steps / dt
+    sample = (f"{rows} of {w.nobs} observations x {w.ntasks} tasks x {w.nf} features per step, {w.dtype}"
+              + (", one gradient pass of the fit" if w.kind == "fit" else ""))
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": workload_config(args, args.gpus),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic", "config": workload_config(w, args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": pyoracle.get_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -224,38 +314,88 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------
-# our arm
+# synthetic data, generated on the device
 # --------------------------------------------------------------------------
-def make_shard(args, rank, world, device):
-    """This rank's rows of the global synthetic problem; blocks of 2^16 rows
-    are seeded by their global index, so the data do not depend on N."""
+def make_local(w: Workload, rank: int, world: int, seed: int, device):
+    """This rank's part of the global synthetic problem.  Blocks of rows
+    (per task) are seeded by their global index, so the data a rank holds do
+    not depend on the number of ranks."""
     import torch
 
-    nobs, nf = args.nobs, args.nfeatures
-    blk = 1 << 16
-    assert nobs % (world * blk) == 0, "nobs must split into 2^16-row blocks per rank"
-    per = nobs // world
+    from gpu_algos_b200.sharded import obs_range, task_range
+
+    dt = torch.float32 if w.dtype == "f32" else torch.float64
+    if w.shard == "obs":
+        assert w.nobs % (world * w.block) == 0, "nobs must split into whole generation blocks per rank"
+        lo, hi = obs_range(w.nobs, world, rank)
+        t_lo, t_hi = 0, w.ntasks
+    elif w.shard == "tasks":
+        lo, hi = 0, w.nobs
+        t_lo, t_hi = task_range(w.ntasks, world, rank)
+    else:
+        lo, hi, t_lo, t_hi = 0, w.nobs, 0, w.ntasks
     g = torch.Generator(device=device)
-    g.manual_seed(args.seed)
-    beta = torch.randn((1, 1, nf), generator=g, device=device, dtype=torch.float32)
-    X = torch.empty((per, 1, nf), device=device, dtype=torch.float32)
-    Y = torch.empty((per, 1, 1), device=device, dtype=torch.float32)
-    for i in range(per // blk):
-        gb = rank * (per // blk) + i
-        g.manual_seed(args.seed * 1_000_003 + gb)
-        xs = X[i * blk:(i + 1) * blk]
-        xs.uniform_(-1.0, 1.0, generator=g)
-        noise = torch.randn((blk,), generator=g, device=device, dtype=torch.float32) * 0.1
-        Y[i * blk:(i + 1) * blk, 0, 0] = xs[:, 0, :] @ beta[0, 0] + noise
-    return X, Y, beta
+    g.manual_seed(seed)
+    beta_true = torch.randn((w.ntasks, w.nt, w.nf), generator=g, device=device, dtype=torch.float64)
+    if w.sparsity < 1:
+        keep = torch.rand((w.ntasks, w.nt, w.nf), generator=g, device=device, dtype=torch.float64) < w.sparsity
+        beta_true = beta_true * keep
+    beta_eval = (torch.randn((w.ntasks, w.nt, w.nf), generator=g, device=device, dtype=torch.float64)
+                 if w.independent_beta else beta_true.clone())
+    nloc, tloc = hi - lo, t_hi - t_lo
+    X = torch.empty((nloc, tloc, w.nf), device=device, dtype=dt)
+    Y = torch.empty((nloc, tloc, w.nt), device=device, dtype=dt)
+    for j in range(tloc):
+        task = t_lo + j
+        bt = beta_true[task].to(dt)  # (nt, nf)
+        for b0 in range(lo, hi, w.block):
+            rows = min(w.block, hi - b0)
+            g.manual_seed(seed * 1_000_003 + task * 1_000_000_007 + b0 // w.block)
+            xs = torch.empty((rows, w.nf), device=device, dtype=dt)
+            if w.x == "uniform":
+                xs.uniform_(-1.0, 1.0, generator=g)
+            else:
+                xs.normal_(generator=g)
+            noise = torch.randn((rows, w.nt), generator=g, device=device, dtype=dt) * w.noise
+            X[b0 - lo:b0 - lo + rows, j, :] = xs
+            Y[b0 - lo:b0 - lo + rows, j, :] = xs @ bt.T + noise
+    M = beta_eval[t_lo:t_hi].to(dt).contiguous()
+    return X, Y, M, (lo, hi, t_lo, t_hi)
 
 
+def measured_fp64_tflops(device):
+    """cuBLAS DGEMM throughput measured here (the FP64 roofline denominator;
+    MEASURED_PEAKS.json has no FP64 figure)."""
+    import torch
+
+    n = 8192
+    a = torch.randn((n, n), device=device, dtype=torch.float64)
+    b = torch.randn((n, n), device=device, dtype=torch.float64)
+    torch.matmul(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.matmul(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     from gpu_algos_b200 import capi, glm
+    from gpu_algos_b200.sharded import CudaBackend, ShardedGLM
 
+    w = args.w
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -266,38 +406,61 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     n_gpus = world
+    collective = world > 1 and w.shard == "obs"
 
-    X, Y, beta = make_shard(args, rank, world, device)
-    nobs_local, _, nf = X.shape
-    ws = torch.empty(glm.workspace_bytes(torch.float32, nf, 1, 1, nobs_local) + 256, dtype=torch.uint8, device=device)
-    grad = torch.empty((1, 1, nf), dtype=torch.float32, device=device)
-    partial = torch.empty((1, 1, nf), dtype=torch.float64, device=device)
+    X, Y, M, _ = make_local(w, rank, world, args.seed, device)
+    nobs_l, ntasks_l, nf = X.shape
+    nt = Y.shape[2]
+    dt = X.dtype
+    esize = X.element_size()
+    ws_bytes = glm.workspace_bytes(dt, nf, nt, ntasks_l, nobs_l)
+    if w.kind == "fit":
+        ws_bytes = max(ws_bytes, int(getattr(capi.lib(), f"glmb_fit_workspace_size_{glm.SUFFIX[dt]}")(
+            nf, nt, ntasks_l, nobs_l)))
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=device)
+    grad = torch.empty((ntasks_l, nt, nf), dtype=dt, device=device)
+    partial = torch.empty((ntasks_l, nt, nf), dtype=torch.float64, device=device)
+    beta_fit = torch.empty((ntasks_l, nt, nf), dtype=dt, device=device)
+    lip = torch.empty((ntasks_l,), dtype=torch.float64, device=device)
     stream = torch.cuda.current_stream()
-    lam = args.lam
-
-    from gpu_algos_b200.sharded import CudaBackend, ShardedGLM
-
     backend = CudaBackend(workspace=ws)
 
-    def step(ev=None):
+    def gradient_step(Xs, Ys, ev=None):
         if ev is not None:
             ev[0].record(stream)
-        if world == 1:
-            glm.gradient(X, beta, Y, lam, 0.0, True, out=grad, workspace=ws)
+        if not collective:
+            glm.gradient(Xs, M, Ys, w.lam, w.alpha, True, out=grad, workspace=ws)
             if ev is not None:
                 ev[1].record(stream)
         else:
-            backend.partial(X, beta, Y, out=partial)
+            backend.partial(Xs, M, Ys, out=partial)
             if ev is not None:
                 ev[1].record(stream)
             dist.all_reduce(partial, op=dist.ReduceOp.SUM)
-            backend.finalize(partial, beta, lam, 0.0, grad)
+            backend.finalize(partial, M, w.lam, w.alpha, grad)
 
+    def fit_step(Xs, Ys, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        if world == 1:
+            glm.fit_elastic_net(Xs, Ys, w.lambda1, w.lambda2, w.n_power, w.n_iter, seed=args.seed,
+                                beta=beta_fit, lipschitz=lip, workspace=ws)
+        else:
+            b, L = ShardedGLM(Xs, Ys, backend).fit_elastic_net(w.lambda1, w.lambda2, w.n_power, w.n_iter,
+                                                               seed=args.seed)
+            beta_fit.copy_(b)
+            lip.copy_(L)
+        if ev is not None:
+            ev[1].record(stream)
+
+    step = fit_step if w.kind == "fit" else gradient_step
+
+    fp64_peak = measured_fp64_tflops(device) if (w.dtype == "f64" and rank == 0) else None
     props = torch.cuda.get_device_properties(device)
     sampler = ClockSampler(f"GPU-{props.uuid}")
 
     for _ in range(args.warmup):
-        step()
+        step(X, Y)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -311,7 +474,7 @@ def run_ours(args):
     t_wall0 = time.time()
     start.record(stream)
     for k in range(args.steps):
-        step(kernel_events[k])
+        step(X, Y, kernel_events[k])
     end.record(stream)
     torch.cuda.synchronize()
     t_wall1 = time.time()
@@ -326,27 +489,27 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total, kernel_ms = float(t[0]), float(t[1])
     ms_per_step = ms_total / args.steps
-    value = args.nobs * nf / (ms_per_step * 1e-3)
+    passes = passes_per_step(w)
+    units_per_pass = w.nobs * w.ntasks * w.nf * (world if w.shard == "replica" else 1)
+    value = units_per_pass * passes / (ms_per_step * 1e-3)
 
     # end to end through the public API from pinned host buffers
     e2e = None
-    if not args.no_e2e:
-        Xh = torch.empty(X.shape, dtype=X.dtype, pin_memory=True)
-        Yh = torch.empty(Y.shape, dtype=Y.dtype, pin_memory=True)
+    if not args.no_e2e and X.numel() * esize <= HOST_PIN_LIMIT:
+        Xh = torch.empty(X.shape, dtype=dt, pin_memory=True)
+        Yh = torch.empty(Y.shape, dtype=dt, pin_memory=True)
         Xh.copy_(X)
         Yh.copy_(Y)
-        gh = torch.empty(grad.shape, dtype=grad.dtype, pin_memory=True)
+        out = beta_fit if w.kind == "fit" else grad
+        oh = torch.empty(out.shape, dtype=dt, pin_memory=True)
         Xd = torch.empty_like(X)
         Yd = torch.empty_like(Y)
 
         def e2e_step():
             Xd.copy_(Xh, non_blocking=True)
             Yd.copy_(Yh, non_blocking=True)
-            if world == 1:
-                glm.gradient(Xd, beta, Yd, lam, 0.0, True, out=grad, workspace=ws)
-            else:
-                ShardedGLM(Xd, Yd, backend).gradient(beta, lam, 0.0, out=grad)
-            gh.copy_(grad, non_blocking=True)
+            step(Xd, Yd)
+            oh.copy_(out, non_blocking=True)
 
         e2e_step()
         torch.cuda.synchronize()
@@ -354,20 +517,21 @@ def run_ours(args):
             dist.barrier()
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
+        n_e2e = max(1, min(args.e2e_steps, args.steps))
         s0.record(stream)
-        for _ in range(args.e2e_steps):
+        for _ in range(n_e2e):
             e2e_step()
         s1.record(stream)
         torch.cuda.synchronize()
         te = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_ms = float(te[0]) / args.e2e_steps
-        e2e = {"value": args.nobs * nf / (e2e_ms * 1e-3), "unit": UNIT,
-               "h2d_bytes_per_step": int(Xh.numel() * 4 + Yh.numel() * 4),
-               "d2h_bytes_per_step": int(gh.numel() * 4), "ms_per_step": e2e_ms,
-               "steps": args.e2e_steps,
-               "path": "pinned host X,Y -> device (cudaMemcpyAsync) -> glmb_gradient_f32 -> host grad"}
+        e2e_ms = float(te[0]) / n_e2e
+        e2e = {"value": units_per_pass * passes / (e2e_ms * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": int((Xh.numel() + Yh.numel()) * esize),
+               "d2h_bytes_per_step": int(oh.numel() * esize), "ms_per_step": e2e_ms, "steps": n_e2e,
+               "path": "pinned host X,Y -> device (cudaMemcpyAsync) -> "
+                       + ("glmb_fit_elastic_net" if w.kind == "fit" else "glmb_gradient") + " -> host result"}
         del Xh, Yh, Xd, Yd
 
     sampler.stop()
@@ -376,29 +540,47 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     if rank == 0:
-        peak, peak_kind = measured_hbm_peak()
-        bytes_launch = algorithmic_bytes(nobs_local, nf)
-        achieved = bytes_launch / (kernel_ms * 1e-3) / 1e9
-        tpr = dram_traffic_per_row()
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                    if peak_kind == "measured" else "fallback 6650 GB/s",
-                    "traffic": (tpr * nobs_local) if tpr is not None else None,
-                    "algorithmic_bytes": bytes_launch, "kernel_ms": kernel_ms,
-                    "kernel": "glm_rows_kernel<float,4,1,1> + glm_finalize_kernel (one glmb_gradient_f32 call)"}
+        hbm_peak, peak_kind = measured_hbm_peak()
+        bytes_pass = algorithmic_bytes(nobs_l, nf, nt, ntasks_l, esize)
+        hbm_achieved = bytes_pass * passes / (kernel_ms * 1e-3) / 1e9
+        tpr = dram_traffic_per_row(w)
+        peak_note = ("measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s")
+        kernel_name = {"gradient": "glm_rows_kernel (+ finalize): one glmb_gradient call",
+                       "driver": "glm_rows_kernel (+ finalize): one glmb_gradient call",
+                       "multitask": "glm_tiles_f64_kernel (+ finalize): one glmb_gradient_f64 call",
+                       "fit": f"whole fit: {passes} passes of glm_rows_kernel + finalize/prox kernels"}[w.name]
+        if collective and w.kind == "gradient":
+            kernel_name = "glm_rows_kernel (+ partial reduction): one glmb_gradient_partial call"
+        if w.name == "multitask":
+            flops = 4.0 * nobs_l * ntasks_l * nf * nt
+            achieved = flops / (kernel_ms * 1e-3) / 1e12
+            roofline = {"bound": "tensor", "achieved": achieved, "peak": fp64_peak, "unit": "TFLOP/s",
+                        "frac": achieved / fp64_peak,
+                        "peak_kind": "measured here: cuBLAS DGEMM 8192^3 (FP64; MEASURED_PEAKS.json has none)",
+                        "traffic": None, "algorithmic_flops": flops, "kernel_ms": kernel_ms, "kernel": kernel_name,
+                        "hbm_achieved_gbs": hbm_achieved, "hbm_frac": hbm_achieved / hbm_peak}
+        else:
+            roofline = {"bound": "hbm", "achieved": hbm_achieved, "peak": hbm_peak, "unit": "GB/s",
+                        "frac": hbm_achieved / hbm_peak, "peak_kind": peak_note,
+                        "traffic": (tpr * nobs_l) if tpr is not None else None,
+                        "algorithmic_bytes": bytes_pass * passes, "kernel_ms": kernel_ms, "kernel": kernel_name}
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n_gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": workload_config(args, n_gpus), "roofline": roofline,
-                "gpu_launches": int(launches), "clocks": clocks}
+                "scaling": "strong" if w.shard != "replica" else "weak", "vs_baseline": None,
+                "dtype": w.dtype, "data": "synthetic", "config": workload_config(w, n_gpus),
+                "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks}
+        if w.kind == "fit":
+            line["fit"] = {"passes_per_step": passes, "ms_per_pass": ms_per_step / passes,
+                           "lipschitz": float(lip[0].item()), "nonzero": int((beta_fit != 0).sum().item())}
         if e2e is not None:
             line["e2e"] = e2e
         if n_gpus == 1 and not args.no_cpu_baseline:
-            rows = min(args.nobs, 1 << 21)
-            rate, cores, secs = cpu_sample_rate(nf, rows, args.lam)
+            rows = cpu_rows(w)
+            rate, cores, secs = cpu_sample_rate(w, rows)
             line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                                    "sample": f"{rows} observations x {nf} features float32, best of 3 "
-                                              f"({secs * 1e3:.1f} ms each)"}
+                                    "sample": f"{rows} observations x {w.ntasks} tasks x {w.nf} features "
+                                              f"{w.dtype}, one pass, best of 3 ({secs * 1e3:.1f} ms each)"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

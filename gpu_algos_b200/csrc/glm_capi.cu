@@ -6,6 +6,10 @@
 //                when ntargets <= 8 and the per-lane accumulators fit in
 //                registers (nfeatures up to 1024 for float, 256 for double
 //                with a single target);
+//   - "tiles":   float64 with up to 16 targets and 256 features that the
+//                rows kernel cannot hold in registers: shared-memory tiles
+//                filled by cp.async.bulk, both contractions on the FP64
+//                tensor pipe (glm_tiles.cu);
 //   - "generic": two-pass kernels (glm_generic.cu) for every other shape and
 //                for half and integer types.
 // Nothing here falls back to the host: a missing or failing device returns
@@ -17,6 +21,7 @@
 #include "glm_fit.cuh"
 #include "glm_generic.cuh"
 #include "glm_rows.cuh"
+#include "glm_tiles.cuh"
 
 namespace glmb {
 
@@ -112,6 +117,12 @@ size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
         if (a.ok) need = std::max(need, round_up(a.part_doubles * sizeof(double), 256));
         if (b.ok) need = std::max(need, round_up(b.part_doubles * sizeof(double), 256));
     }
+    if constexpr (std::is_same_v<T, double>) {
+        if (!all_rows && tiles_f64_supported(nf, nt, ntasks, nullptr)) {
+            const TilesPlan tp = tiles_f64_plan(nf, nt, ntasks, nobs);
+            need = std::max(need, round_up(tp.part_doubles * sizeof(double), 256) + 256);
+        }
+    }
     if (!all_rows) need = std::max(need, generic_workspace_bytes<T>(nf, nt, ntasks, nobs));
     return need;
 }
@@ -155,6 +166,25 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
             if (st != GLMB_OK) return st;
             return finalize_launch<T, double>(sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M,
                                               grad, partial_out, lambda, alpha, reg, stream);
+        }
+    }
+    if constexpr (std::is_same_v<T, double>) {
+        if (tiles_f64_supported(nf, nt, ntasks, X)) {
+            const TilesPlan tp = tiles_f64_plan(nf, nt, ntasks, nobs);
+            const size_t part_bytes = round_up(tp.part_doubles * sizeof(double), 256);
+            Scratch sc(ws, ws_bytes, part_bytes + 256, stream);
+            if (sc.status() != GLMB_OK) return sc.status();
+            double* part = sc.as<double>();
+            int* status = reinterpret_cast<int*>(sc.as<char>() + part_bytes);
+            cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+            if (e != cudaSuccess) return int(e);
+            set_last_path("tiles");
+            st = tiles_f64_launch(tp, X, M, Yin, Yhat_out, part, status, nf, nt, ntasks, nobs, stream);
+            if (st != GLMB_OK) return st;
+            st = finalize_launch<T, double>(part, tp.ctas_per_task, ntasks * nt * nf, M, grad, partial_out,
+                                            lambda, alpha, reg, stream);
+            if (st != GLMB_OK) return st;
+            return tiles_poison(status, partial_out, partial_out ? nullptr : grad, ntasks * nt * nf, stream);
         }
     }
     set_last_path("generic");

@@ -236,3 +236,31 @@ def test_fit_matches_oracle(dt, oracle):
     b = beta.cpu().numpy()
     assert np.max(np.abs(b - ob)) <= tol * np.max(np.abs(ob))
     assert np.array_equal(b == 0, ob == 0) or dt == np.float32
+
+
+def test_tiles_path_multitask_f64(oracle):
+    # the multi-task float64 shape (64 tasks x 256 features x 16 targets), fewer observations
+    rng = np.random.default_rng(33)
+    nobs, ntasks, nf, nt = 1500, 64, 256, 16
+    X = rng.normal(size=(nobs, ntasks, nf))
+    bt = rng.normal(size=(ntasks, nt, nf))
+    Y = np.einsum("otf,tkf->otk", X, bt) + 0.05 * rng.normal(size=(nobs, ntasks, nt))
+    M = rng.normal(size=(ntasks, nt, nf))
+    g, yh = G.gradient(X, M, Y, lam=0.1, alpha=0.0, reg=True, want_yhat=True)
+    assert capi.last_path() == "tiles"
+    og = oracle.gradient(X, M, Y, 0.1, 0.0, True)
+    # mixed-sign data: elements far below the gradient's scale are compared
+    # relative to 1e-3 of its largest element (cancellation floor)
+    assert G.rel_err(g, og, floor=1e-3 * np.abs(og).max()) <= 1e-11
+    pscale = np.einsum("otf,tkf->otk", np.abs(X), np.abs(M))
+    assert np.all(np.abs(yh - oracle.predict(X, M)) <= 1e-12 * pscale)
+    # ragged tiles and a target count below 8
+    for (nobs, ntasks, nf, nt) in ((33, 3, 10, 9), (100, 2, 256, 12), (70, 5, 64, 16), (45, 1, 2, 16)):
+        X = rng.uniform(0, 1, (nobs, ntasks, nf))
+        M = rng.uniform(0, 1, (ntasks, nt, nf))
+        Y = rng.uniform(0, 1, (nobs, ntasks, nt))
+        g = G.gradient(X, M, Y, 0.2, 0.5, reg=True)
+        assert capi.last_path() == "tiles"
+        assert G.rel_err(g, oracle.gradient(X, M, Y, 0.2, 0.5, True)) <= 1e-11
+        g0 = G.gradient(X, M, None, reg=False)
+        assert G.rel_err(g0, oracle.gradient(X, M, None, with_reg=False)) <= 1e-11
