@@ -404,6 +404,10 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
 
+        # keep stdout for the one JSON line: NCCL's own messages go to stderr
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     n_gpus = world
     collective = world > 1 and w.shard == "obs"
