@@ -96,6 +96,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                   help="cross-GPU sum of the partial gradient: library peer-memory exchange or NCCL all-reduce")
     a = p.parse_args()
     w = WORKLOADS[a.workload]
     if a.nobs is not None:
@@ -111,7 +113,7 @@ def passes_per_step(w: Workload) -> int:
     return (w.n_power + w.n_iter) if w.kind == "fit" else 1
 
 
-def workload_config(w: Workload, n_gpus: int) -> dict:
+def workload_config(w: Workload, n_gpus: int, exchange: str = "peer") -> dict:
     cfg = {
         "workload": (f"glm_{'fit_elastic_net' if w.kind == 'fit' else 'gradient'} {w.dtype} nobs={w.nobs} "
                      f"nfeatures={w.nf} ntargets={w.nt} ntasks={w.ntasks}"),
@@ -129,7 +131,10 @@ def workload_config(w: Workload, n_gpus: int) -> dict:
     if n_gpus == 1:
         cfg["parallelism"] = "single GPU"
     elif w.shard == "obs":
-        cfg["parallelism"] = f"obs-sharded x{n_gpus} + one NCCL all-reduce of the partial gradient per pass"
+        cfg["parallelism"] = (f"obs-sharded x{n_gpus} + one NCCL all-reduce of the partial gradient per pass"
+                              if exchange == "nccl" else
+                              f"obs-sharded x{n_gpus}; partials summed over NVLink peer memory by the "
+                              "library's exchange kernel (P2P stores + flags), one per pass")
     elif w.shard == "tasks":
         cfg["parallelism"] = f"tasks-sharded x{n_gpus}, no collective"
     else:
@@ -427,13 +432,24 @@ def run_ours(args):
     beta_fit = torch.empty((ntasks_l, nt, nf), dtype=dt, device=device)
     lip = torch.empty((ntasks_l,), dtype=torch.float64, device=device)
     stream = torch.cuda.current_stream()
-    backend = CudaBackend(workspace=ws)
+    peer = None
+    if collective and args.exchange == "peer":
+        from gpu_algos_b200.sharded import PeerBackend, PeerGroup
+
+        peer = PeerGroup(max_elems=ntasks_l * nt * nf, timeout_ms=5000.0)
+        backend = PeerBackend(peer, workspace=ws)
+    else:
+        backend = CudaBackend(workspace=ws)
 
     def gradient_step(Xs, Ys, ev=None):
         if ev is not None:
             ev[0].record(stream)
         if not collective:
             glm.gradient(Xs, M, Ys, w.lam, w.alpha, True, out=grad, workspace=ws)
+            if ev is not None:
+                ev[1].record(stream)
+        elif peer is not None:
+            backend.reduced_gradient(Xs, M, Ys, w.lam, w.alpha, grad, None)
             if ev is not None:
                 ev[1].record(stream)
         else:
@@ -451,7 +467,7 @@ def run_ours(args):
                                 beta=beta_fit, lipschitz=lip, workspace=ws)
         else:
             b, L = ShardedGLM(Xs, Ys, backend).fit_elastic_net(w.lambda1, w.lambda2, w.n_power, w.n_iter,
-                                                               seed=args.seed)
+                                                               seed=args.seed)  # peer or NCCL exchange
             beta_fit.copy_(b)
             lip.copy_(L)
         if ev is not None:
@@ -555,7 +571,9 @@ def run_ours(args):
                        "multitask": "glm_tiles_f64_kernel (+ finalize): one glmb_gradient_f64 call",
                        "fit": f"whole fit: {passes} passes of glm_rows_kernel + finalize/prox kernels"}[w.name]
         if collective and w.kind == "gradient":
-            kernel_name = "glm_rows_kernel (+ partial reduction): one glmb_gradient_partial call"
+            kernel_name = ("glm_rows_kernel + glm_exchange_kernel: one glmb_gradient_sharded call"
+                           if peer is not None else
+                           "glm_rows_kernel (+ partial reduction): one glmb_gradient_partial call")
         if w.name == "multitask":
             flops = 4.0 * nobs_l * ntasks_l * nf * nt
             achieved = flops / (kernel_ms * 1e-3) / 1e12
@@ -572,7 +590,7 @@ def run_ours(args):
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n_gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
                 "scaling": "strong" if w.shard != "replica" else "weak", "vs_baseline": None,
-                "dtype": w.dtype, "data": "synthetic", "config": workload_config(w, n_gpus),
+                "dtype": w.dtype, "data": "synthetic", "config": workload_config(w, n_gpus, args.exchange),
                 "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks}
         if w.kind == "fit":
             line["fit"] = {"passes_per_step": passes, "ms_per_pass": ms_per_step / passes,
@@ -587,6 +605,11 @@ def run_ours(args):
                                               f"{w.dtype}, one pass, best of 3 ({secs * 1e3:.1f} ms each)"}
         print(json.dumps(line), flush=True)
     if world > 1:
+        dist.barrier()
+        if peer is not None:
+            if peer.status() != 0:
+                print("[bench] a peer exchange wait ran out", file=sys.stderr)
+            peer.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

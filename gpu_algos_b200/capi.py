@@ -20,6 +20,8 @@ GLMB_ERR_WORKSPACE = 1002
 GLMB_ERR_UNSUPPORTED = 1003
 GLMB_ERR_TOO_LARGE = 1004
 
+PEER_HANDLE_BYTES = 64
+
 GRAD_REGULARIZE = 0x1
 GRAD_WRITE_YHAT = 0x2
 GRAD_Y_ZERO = 0x4
@@ -82,6 +84,20 @@ def _declare(L: ctypes.CDLL) -> None:
         f.restype = _SZ
     L.glmb_gradient_noalloc_f32.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P]
     L.glmb_gradient_noalloc_f32.restype = _INT
+    L.glmb_peer_group_create.argtypes = [_INT, _INT, _I64, _D, ctypes.POINTER(ctypes.c_void_p), _P]
+    L.glmb_peer_group_connect.argtypes = [_P, _P]
+    L.glmb_peer_group_connect_local.argtypes = [_P, ctypes.POINTER(ctypes.c_void_p)]
+    L.glmb_peer_group_buffer.argtypes = [_P]
+    L.glmb_peer_group_buffer.restype = _P
+    L.glmb_peer_group_status.argtypes = [_P, ctypes.POINTER(ctypes.c_int), _INT]
+    L.glmb_peer_group_destroy.argtypes = [_P]
+    for name in ("glmb_peer_group_create", "glmb_peer_group_connect", "glmb_peer_group_connect_local",
+                 "glmb_peer_group_status", "glmb_peer_group_destroy"):
+        getattr(L, name).restype = _INT
+    for s in FLOATING:
+        f = getattr(L, f"glmb_gradient_sharded_{s}")
+        f.argtypes = [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P, _P, _SZ, _P]
+        f.restype = _INT
 
 
 def lib() -> ctypes.CDLL:
@@ -135,4 +151,7 @@ def exported_symbols() -> list[str]:
                   f"glmb_prox_update_{s}", f"glmb_power_step_{s}", f"glmb_power_init_{s}",
                   f"glmb_fit_workspace_size_{s}", f"glmb_fit_elastic_net_{s}"]
     names.append("glmb_gradient_noalloc_f32")
+    names += ["glmb_peer_group_create", "glmb_peer_group_connect", "glmb_peer_group_connect_local",
+              "glmb_peer_group_buffer", "glmb_peer_group_status", "glmb_peer_group_destroy"]
+    names += [f"glmb_gradient_sharded_{s}" for s in FLOATING]
     return names

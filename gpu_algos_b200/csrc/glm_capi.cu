@@ -20,6 +20,7 @@
 #include "glm_common.cuh"
 #include "glm_fit.cuh"
 #include "glm_generic.cuh"
+#include "glm_peer.cuh"
 #include "glm_rows.cuh"
 #include "glm_tiles.cuh"
 
@@ -130,9 +131,30 @@ size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
 // Shared body of glmb_gradient_* (partial_out == NULL) and
 // glmb_gradient_partial_* (partial_out != NULL, grad unused).
 template <typename T>
+struct PeerFinish {
+    glmb_peer_group* g;
+    const T* M;
+    T* grad;
+    double* partial_out;
+    double lambda, alpha;
+    bool reg;
+    const int* local_status;
+    int64_t total;
+    cudaStream_t stream;
+    static int call(void* ctx, const void* part, int64_t nparts) {
+        auto* f = static_cast<PeerFinish*>(ctx);
+        return exchange_launch<T>(f->g, static_cast<const double*>(part), nparts, f->total, f->M, f->grad,
+                                  f->partial_out, f->lambda, f->alpha, f->reg, f->local_status, f->stream);
+    }
+};
+
+// With `peer` set (float/double only), the CTA partials are summed across
+// the ranks of the group by the exchange kernel instead of the local finalize.
+template <typename T>
 int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
                   int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda, double alpha,
-                  uint32_t flags, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                  uint32_t flags, void* ws, size_t ws_bytes, cudaStream_t stream,
+                  glmb_peer_group* peer = nullptr) {
     if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0) return GLMB_ERR_INVALID_VALUE;
     if (flags & ~(GLMB_GRAD_REGULARIZE | GLMB_GRAD_WRITE_YHAT | GLMB_GRAD_Y_ZERO))
         return GLMB_ERR_INVALID_VALUE;
@@ -164,6 +186,11 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
             set_last_path("rows");
             st = rows_launch<T>(p, write_yhat ? kRowsGradYhat : kRowsGrad, a, stream);
             if (st != GLMB_OK) return st;
+            if constexpr (kRowsType<T>) {
+                if (peer != nullptr)
+                    return exchange_launch<T>(peer, sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M, grad,
+                                              partial_out, lambda, alpha, reg, nullptr, stream);
+            }
             return finalize_launch<T, double>(sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M,
                                               grad, partial_out, lambda, alpha, reg, stream);
         }
@@ -181,6 +208,9 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
             set_last_path("tiles");
             st = tiles_f64_launch(tp, X, M, Yin, Yhat_out, part, status, nf, nt, ntasks, nobs, stream);
             if (st != GLMB_OK) return st;
+            if (peer != nullptr)
+                return exchange_launch<T>(peer, part, tp.ctas_per_task, ntasks * nt * nf, M, grad, partial_out,
+                                          lambda, alpha, reg, status, stream);
             st = finalize_launch<T, double>(part, tp.ctas_per_task, ntasks * nt * nf, M, grad, partial_out,
                                             lambda, alpha, reg, stream);
             if (st != GLMB_OK) return st;
@@ -188,6 +218,13 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
         }
     }
     set_last_path("generic");
+    if constexpr (kRowsType<T>) {
+        if (peer != nullptr) {
+            PeerFinish<T> fin{peer, M, grad, partial_out, lambda, alpha, reg, nullptr, ntasks * nt * nf, stream};
+            return generic_gradient<T>(X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
+                                       alpha, reg, ws, ws_bytes, stream, &PeerFinish<T>::call, &fin);
+        }
+    }
     return generic_gradient<T>(X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
                                alpha, reg, ws, ws_bytes, stream);
 }
@@ -416,5 +453,43 @@ GLMB_DEFINE_BASIC(u64, uint64_t, uint64_t)
 
 GLMB_DEFINE_FLOATING(f32, float)
 GLMB_DEFINE_FLOATING(f64, double)
+
+int glmb_peer_group_create(int rank, int world, int64_t max_elems, double timeout_ms, glmb_peer_group** group,
+                           void* handle_out) {
+    return guarded([&] { return glmb::peer_group_create(rank, world, max_elems, timeout_ms, group, handle_out); });
+}
+int glmb_peer_group_connect(glmb_peer_group* group, const void* handles) {
+    if (handles == nullptr) return GLMB_ERR_INVALID_VALUE;
+    return guarded([&] { return glmb::peer_group_connect(group, handles, nullptr); });
+}
+int glmb_peer_group_connect_local(glmb_peer_group* group, void* const* peer_buffers) {
+    if (peer_buffers == nullptr) return GLMB_ERR_INVALID_VALUE;
+    return guarded([&] { return glmb::peer_group_connect(group, nullptr, peer_buffers); });
+}
+void* glmb_peer_group_buffer(glmb_peer_group* group) { return glmb::peer_group_buffer(group); }
+int glmb_peer_group_status(glmb_peer_group* group, int* status, int reset) {
+    return guarded([&] { return glmb::peer_group_status(group, status, reset); });
+}
+int glmb_peer_group_destroy(glmb_peer_group* group) {
+    return guarded([&] { return glmb::peer_group_destroy(group); });
+}
+
+#define GLMB_DEFINE_PEER(SFX, T)                                                                    \
+    int glmb_gradient_sharded_##SFX(const T* X, const T* M, const T* Y, T* grad_M, double* partial_out, \
+                                    T* Yhat, int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,  \
+                                    double lambda, double alpha, uint32_t flags, glmb_peer_group* group, \
+                                    void* workspace, size_t workspace_bytes, glmb_stream_t stream) {  \
+        if (group == nullptr) return GLMB_ERR_INVALID_VALUE;                                        \
+        if (partial_out == nullptr && grad_M == nullptr && nf > 0 && nt > 0 && ntasks > 0)          \
+            return GLMB_ERR_INVALID_VALUE;                                                          \
+        return guarded([&] {                                                                        \
+            return glmb::gradient_impl<T>(X, M, Y, partial_out ? nullptr : grad_M, Yhat, partial_out, nf, \
+                                          nt, ntasks, nobs, lambda, alpha, flags, workspace,        \
+                                          workspace_bytes, reinterpret_cast<cudaStream_t>(stream), group); \
+        });                                                                                         \
+    }
+
+GLMB_DEFINE_PEER(f32, float)
+GLMB_DEFINE_PEER(f64, double)
 
 }  // extern "C"

@@ -164,7 +164,8 @@ int finalize_launch(const P* part, int64_t nparts, int64_t total, const T* M, T*
 template <typename T>
 int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
                      int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda,
-                     double alpha, bool reg, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                     double alpha, bool reg, void* ws, size_t ws_bytes, cudaStream_t stream,
+                     PartsFinisher fin, void* fin_ctx) {
     using D = typename Arith<T>::Dot;
     using A = typename Arith<T>::Acc;
     const GenericPlan p = generic_plan<T>(nf, nt, ntasks, nobs);
@@ -187,6 +188,7 @@ int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, doubl
         count_launch();
         if ((st = launch_status()) != GLMB_OK) return st;
     }
+    if (fin != nullptr) return fin(fin_ctx, part, p.nsplit);
     return finalize_launch<T, A>(part, p.nsplit, ntasks * nt * nf, M, grad, partial_out, lambda,
                                  alpha, reg, stream);
 }
@@ -197,7 +199,7 @@ int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, doubl
                                     cudaStream_t);                                                 \
     template int generic_gradient<T>(const T*, const T*, const T*, T*, T*, double*, int64_t,       \
                                      int64_t, int64_t, int64_t, double, double, bool, void*,       \
-                                     size_t, cudaStream_t);
+                                     size_t, cudaStream_t, PartsFinisher, void*);
 
 GLMB_INSTANTIATE_GENERIC(__half)
 GLMB_INSTANTIATE_GENERIC(float)

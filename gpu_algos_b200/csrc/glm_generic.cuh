@@ -19,10 +19,14 @@ int generic_predict(const T* X, const T* M, T* Yhat, int64_t nf, int64_t nt, int
 // into scratch, then per-(task, feature-block, obs-split) sums of E*X, then
 // the fixed-order reduction over splits.  With partial_out != NULL the
 // reduction writes sum (Yhat - Y) X as double instead of the gradient.
+// With `fin` set, fin(fin_ctx, part, nparts) replaces that reduction: part is
+// laid out [e][nparts] in the Acc type (double for float/double inputs).
+using PartsFinisher = int (*)(void* ctx, const void* part, int64_t nparts);
 template <typename T>
 int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
                      int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda,
-                     double alpha, bool reg, void* ws, size_t ws_bytes, cudaStream_t stream);
+                     double alpha, bool reg, void* ws, size_t ws_bytes, cudaStream_t stream,
+                     PartsFinisher fin = nullptr, void* fin_ctx = nullptr);
 
 // Reduction of per-part sums part[e * nparts + c] over c in a fixed order, one
 // warp per output element e < total, then either

@@ -1,0 +1,252 @@
+// glm_peer.cu -- observation-sharded gradient with the cross-GPU sum done
+// over NVLink peer memory inside one kernel.
+//
+// Every rank owns a "symmetric" buffer (the same layout on each GPU):
+//   slots[2][world][max_elems] doubles   (double-buffered by call parity)
+//   flags[world] uint64                   (last call number received per sender)
+// A sharded evaluation is two launches per rank:
+//   1. the usual CTA-partial kernel over the local observations
+//      (glm_rows_kernel / glm_tiles_f64_kernel / the generic pair);
+//   2. glm_exchange_kernel, one CTA: sums the CTA partials in a fixed order,
+//      stores the rank's partial into slot [parity][rank] of every peer's
+//      buffer (plain P2P stores over NVLink), publishes flag[rank] = call
+//      number with a system-scope release, waits (bounded) until every
+//      sender's flag in its own buffer has reached the call number, sums the
+//      world slots in rank order -- so every rank obtains bit-identical
+//      results -- and applies the elastic-net finalize (or writes the summed
+//      partial for the optimizer).
+// Slots alternate with the call parity: a sender can be at most one call
+// ahead of a receiver still reading, so two slot sets never collide.
+//
+// Waits are bounded by a clock budget (timeout_ms at group creation): on
+// expiry the kernel sets the group's status word, writes NaN outputs and
+// returns; the host reads the status with glmb_peer_group_status.
+#include <cmath>
+#include <cstring>
+#include <new>
+
+#include "glm_common.cuh"
+#include "glm_peer.cuh"
+
+struct glmb_peer_group {
+    int rank = 0, world = 0, device = 0;
+    int64_t max_elems = 0;
+    size_t bytes = 0;
+    void* buf = nullptr;               // own symmetric buffer (cudaMalloc)
+    void* peers[GLMB_PEER_MAX_WORLD];  // peer base pointers (own buf at [rank])
+    bool opened[GLMB_PEER_MAX_WORLD];  // pointer came from cudaIpcOpenMemHandle
+    void** d_peers = nullptr;          // device copy of peers[]
+    int* d_status = nullptr;
+    uint64_t epoch = 0;
+    long long timeout_cycles = 0;
+    bool connected = false;
+};
+
+namespace glmb {
+
+namespace {
+
+constexpr int kExThreads = 1024;
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct ExArgs {
+    const double* part;  // [e][nparts]
+    int64_t nparts, total, max_elems;
+    void* const* peers;  // device array: base pointer of every rank's buffer
+    int rank, world;
+    uint64_t epoch;
+    long long timeout_cycles;
+    int* status;
+    const int* local_status;  // the partial kernel's own status word, or NULL
+    double lambda, alpha;
+    int reg;
+};
+
+__device__ __forceinline__ double* slot_of(void* base, int parity, int sender, int world, int64_t max_elems) {
+    return static_cast<double*>(base) + (int64_t(parity) * world + sender) * max_elems;
+}
+__device__ __forceinline__ uint64_t* flags_of(void* base, int world, int64_t max_elems) {
+    return reinterpret_cast<uint64_t*>(static_cast<double*>(base) + 2 * int64_t(world) * max_elems);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kExThreads)
+    glm_exchange_kernel(const ExArgs a, const T* __restrict__ M, T* __restrict__ grad, double* __restrict__ partial_out) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = kExThreads / 32;
+    const int parity = int(a.epoch & 1);
+    void* own = a.peers[a.rank];
+    double* mine = slot_of(own, parity, a.rank, a.world, a.max_elems);
+
+    // 1. this rank's partial: fixed-order sum of the CTA partials
+    for (int64_t e = warp; e < a.total; e += nwarps) {
+        double s = 0.0;
+        for (int64_t c = lane; c < a.nparts; c += 32) s += a.part[e * a.nparts + c];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (lane == 0) mine[e] = s;
+    }
+    __syncthreads();
+    // 2. push it into the same slot of every peer's buffer
+    for (int p = 0; p < a.world; ++p) {
+        if (p == a.rank) continue;
+        double* dst = slot_of(a.peers[p], parity, a.rank, a.world, a.max_elems);
+        for (int64_t e = tid; e < a.total; e += kExThreads) dst[e] = mine[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < a.world) st_release_sys(flags_of(a.peers[tid], a.world, a.max_elems) + a.rank, a.epoch);
+
+    // 3. wait until every sender's slot of this call has arrived (bounded)
+    bool failed = false;
+    if (tid < a.world) {
+        const uint64_t* f = flags_of(own, a.world, a.max_elems) + tid;
+        const long long t0 = clock64();
+        while (ld_acquire_sys(f) < a.epoch) {
+            if (clock64() - t0 > a.timeout_cycles) {
+                failed = true;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (a.local_status != nullptr && *a.local_status != 0) failed = true;
+    failed = __syncthreads_or(failed);
+    if (failed) {
+        if (tid == 0) atomicExch(a.status, 1);
+        const double nan = __longlong_as_double(0x7ff8000000000000ll);
+        for (int64_t e = tid; e < a.total; e += kExThreads) {
+            if (partial_out != nullptr) partial_out[e] = nan;
+            else grad[e] = T(nan);
+        }
+        return;
+    }
+    // every thread acquires the flags it depends on before reading the slots
+    for (int r = 0; r < a.world; ++r) (void)ld_acquire_sys(flags_of(own, a.world, a.max_elems) + r);
+
+    // 4. the same rank-ordered sum on every rank, then finalize
+    for (int64_t e = tid; e < a.total; e += kExThreads) {
+        double s = 0.0;
+        for (int r = 0; r < a.world; ++r) s += slot_of(own, parity, r, a.world, a.max_elems)[e];
+        if (partial_out != nullptr) partial_out[e] = s;
+        else grad[e] = finalize_value<T>(s, M[e], a.lambda, a.alpha, a.reg != 0);
+    }
+}
+
+}  // namespace
+
+int peer_group_create(int rank, int world, int64_t max_elems, double timeout_ms, glmb_peer_group** out,
+                      void* handle_out) {
+    if (out == nullptr || world < 1 || world > GLMB_PEER_MAX_WORLD || rank < 0 || rank >= world ||
+        max_elems < 1 || timeout_ms <= 0)
+        return GLMB_ERR_INVALID_VALUE;
+    *out = nullptr;
+    auto* g = new (std::nothrow) glmb_peer_group();
+    if (g == nullptr) return GLMB_ERR_INVALID_VALUE;
+    g->rank = rank;
+    g->world = world;
+    g->max_elems = max_elems;
+    for (int i = 0; i < GLMB_PEER_MAX_WORLD; ++i) {
+        g->peers[i] = nullptr;
+        g->opened[i] = false;
+    }
+    cudaError_t e = cudaGetDevice(&g->device);
+    int clock_khz = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, g->device);
+    g->timeout_cycles = static_cast<long long>(timeout_ms * double(clock_khz > 0 ? clock_khz : 2000000));
+    g->bytes = size_t(2) * world * max_elems * sizeof(double) + size_t(world) * sizeof(uint64_t);
+    if (e == cudaSuccess) e = cudaMalloc(&g->buf, g->bytes);
+    if (e == cudaSuccess) e = cudaMemset(g->buf, 0, g->bytes);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&g->d_peers), sizeof(void*) * GLMB_PEER_MAX_WORLD);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&g->d_status), sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(g->d_status, 0, sizeof(int));
+    if (e == cudaSuccess && handle_out != nullptr) {
+        cudaIpcMemHandle_t h;
+        e = cudaIpcGetMemHandle(&h, g->buf);
+        if (e == cudaSuccess) std::memcpy(handle_out, &h, sizeof(h));
+    }
+    if (e != cudaSuccess) {
+        peer_group_destroy(g);
+        return int(e);
+    }
+    g->peers[rank] = g->buf;
+    *out = g;
+    return GLMB_OK;
+}
+
+int peer_group_connect(glmb_peer_group* g, const void* handles, void* const* local_ptrs) {
+    if (g == nullptr || g->connected || (handles == nullptr && local_ptrs == nullptr)) return GLMB_ERR_INVALID_VALUE;
+    for (int p = 0; p < g->world; ++p) {
+        if (p == g->rank) continue;
+        if (local_ptrs != nullptr) {
+            if (local_ptrs[p] == nullptr) return GLMB_ERR_INVALID_VALUE;
+            g->peers[p] = local_ptrs[p];
+        } else {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const char*>(handles) + size_t(p) * GLMB_PEER_HANDLE_BYTES, sizeof(h));
+            void* ptr = nullptr;
+            const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) return int(e);
+            g->peers[p] = ptr;
+            g->opened[p] = true;
+        }
+    }
+    const cudaError_t e = cudaMemcpy(g->d_peers, g->peers, sizeof(void*) * GLMB_PEER_MAX_WORLD, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return int(e);
+    g->connected = true;
+    return GLMB_OK;
+}
+
+int peer_group_status(glmb_peer_group* g, int* status, int reset) {
+    if (g == nullptr || status == nullptr) return GLMB_ERR_INVALID_VALUE;
+    cudaError_t e = cudaMemcpy(status, g->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && reset) e = cudaMemset(g->d_status, 0, sizeof(int));
+    return int(e);
+}
+
+int peer_group_destroy(glmb_peer_group* g) {
+    if (g == nullptr) return GLMB_OK;
+    int st = GLMB_OK;
+    for (int p = 0; p < GLMB_PEER_MAX_WORLD; ++p)
+        if (g->opened[p]) {
+            const cudaError_t e = cudaIpcCloseMemHandle(g->peers[p]);
+            if (e != cudaSuccess && st == GLMB_OK) st = int(e);
+        }
+    if (g->buf) cudaFree(g->buf);
+    if (g->d_peers) cudaFree(g->d_peers);
+    if (g->d_status) cudaFree(g->d_status);
+    delete g;
+    return st;
+}
+
+void* peer_group_buffer(glmb_peer_group* g) { return g ? g->buf : nullptr; }
+
+template <typename T>
+int exchange_launch(glmb_peer_group* g, const double* part, int64_t nparts, int64_t total, const T* M, T* grad,
+                    double* partial_out, double lambda, double alpha, bool reg, const int* local_status,
+                    cudaStream_t stream) {
+    if (g == nullptr || !g->connected) return GLMB_ERR_INVALID_VALUE;
+    if (total > g->max_elems) return GLMB_ERR_TOO_LARGE;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != g->device) return GLMB_ERR_INVALID_VALUE;
+    ++g->epoch;
+    ExArgs a{part, nparts, total, g->max_elems, g->d_peers, g->rank, g->world, g->epoch, g->timeout_cycles,
+             g->d_status, local_status, lambda, alpha, reg ? 1 : 0};
+    glm_exchange_kernel<T><<<1, kExThreads, 0, stream>>>(a, M, grad, partial_out);
+    count_launch();
+    return launch_status();
+}
+
+template int exchange_launch<float>(glmb_peer_group*, const double*, int64_t, int64_t, const float*, float*, double*,
+                                    double, double, bool, const int*, cudaStream_t);
+template int exchange_launch<double>(glmb_peer_group*, const double*, int64_t, int64_t, const double*, double*,
+                                     double*, double, double, bool, const int*, cudaStream_t);
+
+}  // namespace glmb

@@ -15,9 +15,15 @@ what :func:`task_range` is for.
 The per-rank arithmetic goes through a :class:`Backend`: :class:`CudaBackend`
 calls ``libglm_b200.so``; the CPU tests supply their own backend and run the
 same orchestration on ``gloo`` ranks.
+
+Two exchanges are available: :class:`CudaBackend` sums the rank partials
+with one NCCL all-reduce; :class:`PeerBackend` does the sum inside the
+library, over NVLink peer memory (``glmb_gradient_sharded_*``: the partial
+kernel plus one exchange kernel, no collective library on the path).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -60,6 +66,14 @@ class Backend:
     def prox_update(self, P, beta, lipschitz, lambda1, lambda2):
         raise NotImplementedError
 
+    # Full-data results.  The default is the local partial followed by an
+    # all-reduce over `group`; a backend that exchanges by itself overrides them.
+    def reduced_partial(self, X, M, Y, group):
+        return _all_reduce(self.partial(X, M, Y), group)
+
+    def reduced_gradient(self, X, M, Y, lam, alpha, out, group):
+        return self.finalize(self.reduced_partial(X, M, Y, group), M, lam, alpha, out)
+
 
 class CudaBackend(Backend):
     """The sm_100a kernels of libglm_b200.so."""
@@ -86,6 +100,79 @@ class CudaBackend(Backend):
         return self.glm.prox_update(P, beta, lipschitz, lambda1, lambda2)
 
 
+class PeerGroup:
+    """This rank's member of a library peer-exchange group.
+
+    Creates the rank's exchange buffer, all-gathers the buffers' IPC handles
+    over ``group`` (the only use of torch.distributed) and maps the peers'
+    buffers.  ``max_elems`` bounds nfeatures*ntargets*ntasks of the
+    gradients exchanged; ``timeout_ms`` bounds every wait for a peer.
+    """
+
+    def __init__(self, max_elems: int, timeout_ms: float = 2000.0, group=None):
+        from . import capi
+
+        self.capi = capi
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        handle = ctypes.create_string_buffer(capi.PEER_HANDLE_BYTES)
+        ptr = ctypes.c_void_p()
+        capi.call("glmb_peer_group_create", self.rank, self.world, int(max_elems), float(timeout_ms),
+                  ctypes.byref(ptr), handle)
+        self.ptr = ptr
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        blob = ctypes.create_string_buffer(b"".join(handles), capi.PEER_HANDLE_BYTES * self.world)
+        capi.call("glmb_peer_group_connect", self.ptr, blob)
+
+    def status(self, reset: bool = True) -> int:
+        """0, or 1 when a wait for a peer ran out (the call's outputs are NaN)."""
+        st = ctypes.c_int(0)
+        self.capi.call("glmb_peer_group_status", self.ptr, ctypes.byref(st), int(reset))
+        return st.value
+
+    def close(self):
+        if self.ptr is not None:
+            self.capi.call("glmb_peer_group_destroy", self.ptr)
+            self.ptr = None
+
+
+class PeerBackend(CudaBackend):
+    """CudaBackend whose cross-rank sum runs over NVLink peer memory inside
+    the library (one exchange kernel per evaluation)."""
+
+    def __init__(self, peer: PeerGroup, workspace=None):
+        super().__init__(workspace)
+        self.peer = peer
+
+    def _sharded(self, X, M, Y, grad, partial, lam, alpha, regularize):
+        from . import capi, glm
+
+        sfx = glm.SUFFIX[X.dtype]
+        nobs, ntasks, nf = X.shape
+        nt = M.shape[1]
+        flags = capi.GRAD_REGULARIZE if regularize else 0
+        if Y is None:
+            flags |= capi.GRAD_Y_ZERO
+        ws_ptr, ws_bytes = ((None, 0) if self.workspace is None
+                            else (self.workspace.data_ptr(), self.workspace.numel() * self.workspace.element_size()))
+        capi.call(f"glmb_gradient_sharded_{sfx}", X.data_ptr(), M.data_ptr(), None if Y is None else Y.data_ptr(),
+                  None if grad is None else grad.data_ptr(), None if partial is None else partial.data_ptr(), None,
+                  nf, nt, ntasks, nobs, float(lam), float(alpha), flags, self.peer.ptr, ws_ptr, ws_bytes,
+                  torch.cuda.current_stream().cuda_stream)
+
+    def reduced_partial(self, X, M, Y, group, out=None):
+        ntasks, nt, nf = M.shape
+        if out is None:
+            out = torch.empty((ntasks, nt, nf), dtype=torch.float64, device=X.device)
+        self._sharded(X, M, Y, None, out, 0.0, 0.0, False)
+        return out
+
+    def reduced_gradient(self, X, M, Y, lam, alpha, out, group):
+        self._sharded(X, M, Y, out, None, lam, alpha, True)
+        return out
+
+
 def _all_reduce(t, group):
     if group is not None or (dist.is_available() and dist.is_initialized()):
         if dist.get_world_size(group) > 1:
@@ -108,15 +195,14 @@ class ShardedGLM:
     group: object = None
 
     def partial_sum(self, M, Y=None, y_zero=False):
-        P = self.backend.partial(self.X_local, M, None if y_zero else (self.Y_local if Y is None else Y))
-        return _all_reduce(P, self.group)
+        return self.backend.reduced_partial(self.X_local, M, None if y_zero else (self.Y_local if Y is None else Y),
+                                            self.group)
 
     def gradient(self, M, lam: float, alpha: float, out=None):
         """Full-data gradient 2 sum (Yhat - Y) X + lam(alpha sign M + 2(1-alpha) M)."""
-        P = self.partial_sum(M)
         if out is None:
             out = torch.empty_like(M)
-        return self.backend.finalize(P, M, lam, alpha, out)
+        return self.backend.reduced_gradient(self.X_local, M, self.Y_local, lam, alpha, out, self.group)
 
     def fit_elastic_net(self, lambda1: float, lambda2: float, n_power: int = 20, n_iter: int = 200,
                         seed: int = 42, checkpoint=None, resume=None):
@@ -140,13 +226,11 @@ class ShardedGLM:
             lipschitz = torch.empty((ntasks,), dtype=torch.float64, device=dev)
             self.backend.power_init(v, seed)
             for _ in range(n_power):
-                P = self.backend.partial(self.X_local, v, None)
-                _all_reduce(P, self.group)
+                P = self.backend.reduced_partial(self.X_local, v, None, self.group)
                 self.backend.power_step(P, v, norm, lipschitz, lambda2)
             beta = torch.zeros((ntasks, nt, nf), dtype=dt, device=dev)
         for it in range(start, n_iter):
-            P = self.backend.partial(self.X_local, beta, self.Y_local)
-            _all_reduce(P, self.group)
+            P = self.backend.reduced_partial(self.X_local, beta, self.Y_local, self.group)
             self.backend.prox_update(P, beta, lipschitz, lambda1, lambda2)
             if checkpoint is not None:
                 checkpoint(it + 1, beta, lipschitz)

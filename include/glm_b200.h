@@ -171,6 +171,47 @@ GLMB_DECLARE_SHARDED(f32, float)
 GLMB_DECLARE_SHARDED(f64, double)
 
 /* ------------------------------------------------------------------------
+ * Sharded evaluation with the cross-GPU sum done over NVLink peer memory,
+ * inside the library (no collective library on the path).  No counterpart
+ * in the reference (single-GPU only).  Each rank creates a group (one
+ * device buffer of 2*world*max_elems doubles + world flags, same layout on
+ * every rank), exchanges the opaque handles with its peers by any means
+ * (e.g. an all-gather of GLMB_PEER_HANDLE_BYTES bytes per rank), and
+ * connects.  glmb_gradient_sharded_* then evaluates the full-data gradient
+ * from the rank's block of observations: the fused partial kernel, then one
+ * exchange kernel that stores the rank's partial into every peer's buffer,
+ * waits for all peers (bounded by timeout_ms), sums the partials in rank
+ * order -- bit-identical on every rank -- and finalizes.  All ranks must make
+ * the same sequence of calls.  A wait that runs out sets the group status
+ * (glmb_peer_group_status) and makes that call's outputs NaN.
+ * Single-process multi-GPU callers connect with glmb_peer_group_connect_local
+ * (peer buffer pointers directly; peer access must be enabled).
+ * ---------------------------------------------------------------------- */
+#define GLMB_PEER_HANDLE_BYTES 64
+#define GLMB_PEER_MAX_WORLD 64
+typedef struct glmb_peer_group glmb_peer_group;
+
+int glmb_peer_group_create(int rank, int world, int64_t max_elems, double timeout_ms,
+                           glmb_peer_group** group, void* handle_out);
+int glmb_peer_group_connect(glmb_peer_group* group, const void* handles /* world x 64 bytes */);
+int glmb_peer_group_connect_local(glmb_peer_group* group, void* const* peer_buffers);
+void* glmb_peer_group_buffer(glmb_peer_group* group);
+int glmb_peer_group_status(glmb_peer_group* group, int* status, int reset);
+int glmb_peer_group_destroy(glmb_peer_group* group);
+
+#define GLMB_DECLARE_PEER(SFX, T)                                                       \
+    /* grad (or, if partial_out != NULL, the summed double partial) of all ranks' */    \
+    int glmb_gradient_sharded_##SFX(const T* X, const T* M, const T* Y, T* grad_M,      \
+                                    double* partial_out, T* Yhat, int64_t nfeatures,    \
+                                    int64_t ntargets, int64_t ntasks, int64_t nobs,     \
+                                    double lambda, double alpha, uint32_t flags,        \
+                                    glmb_peer_group* group, void* workspace,            \
+                                    size_t workspace_bytes, glmb_stream_t stream);
+
+GLMB_DECLARE_PEER(f32, float)
+GLMB_DECLARE_PEER(f64, double)
+
+/* ------------------------------------------------------------------------
  * Elastic-net proximal gradient (ISTA).  No counterpart in the reference,
  * which ships the gradient's elastic-net term
  * (include/cuda/kernels/glm/glm_gradient_xyyhat.cuh:197-211) but no optimizer.

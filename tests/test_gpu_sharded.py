@@ -28,11 +28,11 @@ def _problem(dt):
     return X, Y, M
 
 
-def _worker(rank, world, port, outdir, dt_name):
+def _worker(rank, world, port, outdir, dt_name, exchange):
     import torch.distributed as dist
     from datetime import timedelta
 
-    from gpu_algos_b200.sharded import CudaBackend, ShardedGLM, obs_range
+    from gpu_algos_b200.sharded import CudaBackend, PeerBackend, PeerGroup, ShardedGLM, obs_range
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -41,11 +41,16 @@ def _worker(rank, world, port, outdir, dt_name):
     try:
         X, Y, M = _problem(np.dtype(dt_name))
         lo, hi = obs_range(X.shape[0], world, rank)
+        peer = PeerGroup(max_elems=M.size, timeout_ms=5000.0) if exchange == "peer" else None
+        backend = PeerBackend(peer) if peer is not None else CudaBackend()
         sh = ShardedGLM(torch.from_numpy(X[lo:hi].copy()).cuda(), torch.from_numpy(Y[lo:hi].copy()).cuda(),
-                        CudaBackend())
+                        backend)
         g = sh.gradient(torch.from_numpy(M).cuda(), 0.2, 0.3)
         beta, lip = sh.fit_elastic_net(50.0, 5.0, n_power=20, n_iter=40, seed=11)
         torch.cuda.synchronize()
+        if peer is not None:
+            assert peer.status() == 0
+            peer.close()
         np.save(os.path.join(outdir, f"g{rank}.npy"), g.cpu().numpy())
         np.save(os.path.join(outdir, f"b{rank}.npy"), beta.cpu().numpy())
         np.save(os.path.join(outdir, f"l{rank}.npy"), lip.cpu().numpy())
@@ -54,14 +59,15 @@ def _worker(rank, world, port, outdir, dt_name):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("dt", [np.float32, np.float64])
-def test_two_gpu_sharded_matches_single_gpu(dt):
+def test_two_gpu_sharded_matches_single_gpu(dt, exchange):
     outdir = tempfile.mkdtemp()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, outdir, np.dtype(dt).name)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, outdir, np.dtype(dt).name, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
