@@ -46,7 +46,7 @@ def _sharded(g, X, M, Y, lam, alpha, partial=False):
 
 
 def test_single_rank_group_equals_plain_gradient():
-    g = _group(0, 1, 4096, 1000.0)
+    g = _group(0, 1, 1 << 15, 1000.0)
     try:
         capi.call("glmb_peer_group_connect_local", g, (ctypes.c_void_p * 1)(capi.lib().glmb_peer_group_buffer(g)))
         rng = np.random.default_rng(2)
