@@ -3,24 +3,27 @@
 //
 // Every rank owns a "symmetric" buffer (the same layout on each GPU):
 //   slots[2][world][max_elems] doubles   (double-buffered by call parity)
-//   flags[world] uint64                   (last call number received per sender)
+//   flags[world][kExMaxBlocks] uint64     (last call number received, per
+//                                          sender and per exchange block)
 // A sharded evaluation is two launches per rank:
 //   1. the usual CTA-partial kernel over the local observations
 //      (glm_rows_kernel / glm_tiles_f64_kernel / the generic pair);
-//   2. glm_exchange_kernel, one CTA: sums the CTA partials in a fixed order,
-//      stores the rank's partial into slot [parity][rank] of every peer's
-//      buffer (plain P2P stores over NVLink), publishes flag[rank] = call
-//      number with a system-scope release, waits (bounded) until every
-//      sender's flag in its own buffer has reached the call number, sums the
-//      world slots in rank order -- so every rank obtains bit-identical
-//      results -- and applies the elastic-net finalize (or writes the summed
-//      partial for the optimizer).
+//   2. glm_exchange_kernel.  Its CTAs split the gradient's elements into
+//      contiguous chunks and work independently: each sums its elements' CTA
+//      partials in a fixed order, stores them into slot [parity][rank] of
+//      every peer's buffer (plain P2P stores over NVLink), publishes
+//      flag[rank][block] = call number with a system-scope release, waits
+//      (bounded) until every sender's flag for its block in its own buffer
+//      has reached the call number, sums the world slots in rank order -- so
+//      every rank obtains bit-identical results -- and applies the
+//      elastic-net finalize (or writes the summed partial for the optimizer).
 // Slots alternate with the call parity: a sender can be at most one call
 // ahead of a receiver still reading, so two slot sets never collide.
 //
 // Waits are bounded by a clock budget (timeout_ms at group creation): on
 // expiry the kernel sets the group's status word, writes NaN outputs and
 // returns; the host reads the status with glmb_peer_group_status.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <new>
@@ -46,7 +49,9 @@ namespace glmb {
 
 namespace {
 
-constexpr int kExThreads = 1024;
+constexpr int kExThreads = 256;
+constexpr int kExMaxBlocks = 64;     // flags per sender
+constexpr int kExElemsPerBlock = 64;  // target chunk (one warp per element, 8 warps)
 
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -73,20 +78,24 @@ struct ExArgs {
 __device__ __forceinline__ double* slot_of(void* base, int parity, int sender, int world, int64_t max_elems) {
     return static_cast<double*>(base) + (int64_t(parity) * world + sender) * max_elems;
 }
-__device__ __forceinline__ uint64_t* flags_of(void* base, int world, int64_t max_elems) {
-    return reinterpret_cast<uint64_t*>(static_cast<double*>(base) + 2 * int64_t(world) * max_elems);
+__device__ __forceinline__ uint64_t* flags_of(void* base, int world, int64_t max_elems, int sender, int block) {
+    return reinterpret_cast<uint64_t*>(static_cast<double*>(base) + 2 * int64_t(world) * max_elems) +
+           int64_t(sender) * kExMaxBlocks + block;
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kExThreads)
     glm_exchange_kernel(const ExArgs a, const T* __restrict__ M, T* __restrict__ grad, double* __restrict__ partial_out) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = kExThreads / 32;
+    const int blk = blockIdx.x, nblk = gridDim.x;
+    const int64_t chunk = (a.total + nblk - 1) / nblk;
+    const int64_t lo = min(a.total, int64_t(blk) * chunk), hi = min(a.total, lo + chunk);
     const int parity = int(a.epoch & 1);
     void* own = a.peers[a.rank];
     double* mine = slot_of(own, parity, a.rank, a.world, a.max_elems);
 
-    // 1. this rank's partial: fixed-order sum of the CTA partials
-    for (int64_t e = warp; e < a.total; e += nwarps) {
+    // 1. this rank's partial for the block's elements: fixed-order sum of the CTA partials
+    for (int64_t e = lo + warp; e < hi; e += nwarps) {
         double s = 0.0;
         for (int64_t c = lane; c < a.nparts; c += 32) s += a.part[e * a.nparts + c];
 #pragma unroll
@@ -94,27 +103,27 @@ __global__ void __launch_bounds__(kExThreads)
         if (lane == 0) mine[e] = s;
     }
     __syncthreads();
-    // 2. push it into the same slot of every peer's buffer
+    // 2. push them into the same slot of every peer's buffer
     for (int p = 0; p < a.world; ++p) {
         if (p == a.rank) continue;
         double* dst = slot_of(a.peers[p], parity, a.rank, a.world, a.max_elems);
-        for (int64_t e = tid; e < a.total; e += kExThreads) dst[e] = mine[e];
+        for (int64_t e = lo + tid; e < hi; e += kExThreads) dst[e] = mine[e];
     }
     __threadfence_system();
     __syncthreads();
-    if (tid < a.world) st_release_sys(flags_of(a.peers[tid], a.world, a.max_elems) + a.rank, a.epoch);
+    if (tid < a.world) st_release_sys(flags_of(a.peers[tid], a.world, a.max_elems, a.rank, blk), a.epoch);
 
-    // 3. wait until every sender's slot of this call has arrived (bounded)
+    // 3. wait until every sender's chunk of this call has arrived (bounded)
     bool failed = false;
     if (tid < a.world) {
-        const uint64_t* f = flags_of(own, a.world, a.max_elems) + tid;
+        const uint64_t* f = flags_of(own, a.world, a.max_elems, tid, blk);
         const long long t0 = clock64();
         while (ld_acquire_sys(f) < a.epoch) {
             if (clock64() - t0 > a.timeout_cycles) {
                 failed = true;
                 break;
             }
-            __nanosleep(64);
+            __nanosleep(32);
         }
     }
     if (a.local_status != nullptr && *a.local_status != 0) failed = true;
@@ -122,17 +131,17 @@ __global__ void __launch_bounds__(kExThreads)
     if (failed) {
         if (tid == 0) atomicExch(a.status, 1);
         const double nan = __longlong_as_double(0x7ff8000000000000ll);
-        for (int64_t e = tid; e < a.total; e += kExThreads) {
+        for (int64_t e = lo + tid; e < hi; e += kExThreads) {
             if (partial_out != nullptr) partial_out[e] = nan;
             else grad[e] = T(nan);
         }
         return;
     }
     // every thread acquires the flags it depends on before reading the slots
-    for (int r = 0; r < a.world; ++r) (void)ld_acquire_sys(flags_of(own, a.world, a.max_elems) + r);
+    for (int r = 0; r < a.world; ++r) (void)ld_acquire_sys(flags_of(own, a.world, a.max_elems, r, blk));
 
     // 4. the same rank-ordered sum on every rank, then finalize
-    for (int64_t e = tid; e < a.total; e += kExThreads) {
+    for (int64_t e = lo + tid; e < hi; e += kExThreads) {
         double s = 0.0;
         for (int r = 0; r < a.world; ++r) s += slot_of(own, parity, r, a.world, a.max_elems)[e];
         if (partial_out != nullptr) partial_out[e] = s;
@@ -161,7 +170,7 @@ int peer_group_create(int rank, int world, int64_t max_elems, double timeout_ms,
     int clock_khz = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, g->device);
     g->timeout_cycles = static_cast<long long>(timeout_ms * double(clock_khz > 0 ? clock_khz : 2000000));
-    g->bytes = size_t(2) * world * max_elems * sizeof(double) + size_t(world) * sizeof(uint64_t);
+    g->bytes = size_t(2) * world * max_elems * sizeof(double) + size_t(world) * glmb::kExMaxBlocks * sizeof(uint64_t);
     if (e == cudaSuccess) e = cudaMalloc(&g->buf, g->bytes);
     if (e == cudaSuccess) e = cudaMemset(g->buf, 0, g->bytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&g->d_peers), sizeof(void*) * GLMB_PEER_MAX_WORLD);
@@ -239,7 +248,9 @@ int exchange_launch(glmb_peer_group* g, const double* part, int64_t nparts, int6
     ++g->epoch;
     ExArgs a{part, nparts, total, g->max_elems, g->d_peers, g->rank, g->world, g->epoch, g->timeout_cycles,
              g->d_status, local_status, lambda, alpha, reg ? 1 : 0};
-    glm_exchange_kernel<T><<<1, kExThreads, 0, stream>>>(a, M, grad, partial_out);
+    // every rank derives the same block count from the same total
+    const int nblk = int(std::max<int64_t>(1, std::min<int64_t>(kExMaxBlocks, (total + kExElemsPerBlock - 1) / kExElemsPerBlock)));
+    glm_exchange_kernel<T><<<nblk, kExThreads, 0, stream>>>(a, M, grad, partial_out);
     count_launch();
     return launch_status();
 }
