@@ -10,6 +10,9 @@
 //                rows kernel cannot hold in registers: shared-memory tiles
 //                filled by cp.async.bulk, both contractions on the FP64
 //                tensor pipe (glm_tiles.cu);
+//   - "dense":   float32 shapes the rows kernel cannot hold (many targets
+//                or features): two TMA-fed tcgen05 GEMMs with 3xTF32
+//                precision (glm_dense.cu);
 //   - "generic": two-pass kernels (glm_generic.cu) for every other shape and
 //                for half and integer types.
 // Nothing here falls back to the host: a missing or failing device returns
@@ -18,6 +21,7 @@
 #include <mutex>
 
 #include "glm_common.cuh"
+#include "glm_dense.cuh"
 #include "glm_fit.cuh"
 #include "glm_generic.cuh"
 #include "glm_peer.cuh"
@@ -118,6 +122,12 @@ size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
         if (a.ok) need = std::max(need, round_up(a.part_doubles * sizeof(double), 256));
         if (b.ok) need = std::max(need, round_up(b.part_doubles * sizeof(double), 256));
     }
+    if constexpr (std::is_same_v<T, float>) {
+        if (!all_rows && dense_f32_supported(nf, nt, ntasks, std::max<int64_t>(nobs, 1), nullptr, nullptr)) {
+            const DensePlan dp = dense_f32_plan(nf, nt, ntasks, std::max<int64_t>(nobs, 1));
+            need = std::max(need, dp.ws_bytes + round_up(size_t(ntasks) * nt * nf * sizeof(double), 256));
+        }
+    }
     if constexpr (std::is_same_v<T, double>) {
         if (!all_rows && tiles_f64_supported(nf, nt, ntasks, nullptr)) {
             const TilesPlan tp = tiles_f64_plan(nf, nt, ntasks, nobs);
@@ -193,6 +203,25 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
             }
             return finalize_launch<T, double>(sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M,
                                               grad, partial_out, lambda, alpha, reg, stream);
+        }
+    }
+    if constexpr (std::is_same_v<T, float>) {
+        if (nobs > 0 && dense_f32_supported(nf, nt, ntasks, nobs, X, M)) {
+            const DensePlan dp = dense_f32_plan(nf, nt, ntasks, nobs);
+            const int64_t total = ntasks * nt * nf;
+            const size_t local_bytes = peer != nullptr ? round_up(size_t(total) * sizeof(double), 256) : 0;
+            Scratch sc(ws, ws_bytes, dp.ws_bytes + local_bytes, stream);
+            if (sc.status() != GLMB_OK) return sc.status();
+            set_last_path("dense");
+            if (peer == nullptr)
+                return dense_f32_gradient(dp, X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
+                                          alpha, reg, sc.as<void>(), stream);
+            double* local = reinterpret_cast<double*>(sc.as<char>() + dp.ws_bytes);
+            st = dense_f32_gradient(dp, X, M, Yin, nullptr, Yhat_out, local, nf, nt, ntasks, nobs, 0.0, 0.0, false,
+                                    sc.as<void>(), stream);
+            if (st != GLMB_OK) return st;
+            return exchange_launch<T>(peer, local, 1, total, M, grad, partial_out, lambda, alpha, reg, nullptr,
+                                      stream);
         }
     }
     if constexpr (std::is_same_v<T, double>) {

@@ -1,0 +1,507 @@
+// glm_dense.cu -- float32 gradient for dense shapes (many targets x many
+// features) on the 5th-generation tensor cores, with 3xTF32 precision.
+//
+// The gradient splits into two GEMMs per task:
+//   GEMM1  R[obs, t] = sum_f X[obs, f] M[t, f] - Y[obs, t]      (K = features)
+//   GEMM2  P_s[t, f] = sum_{obs in split s} R[obs, t] X[obs, f]  (K = observations)
+// followed by a fixed-order double sum over the splits s and the elastic-net
+// finalize.  Both GEMMs run glm_dense_gemm_kernel: TMA (cp.async.bulk.tensor,
+// 128-byte swizzle) stages 128 x 32 and 256 x 32 fp32 tiles into shared
+// memory through a two-stage mbarrier ring; one thread issues
+// tcgen05.mma.kind::tf32 with the accumulator in tensor memory (TMEM, 256
+// columns); four warps read TMEM back with tcgen05.ld for the epilogue.
+//
+// 3xTF32 (Ootomo & Yokota, 2022): a = hi + lo with hi = a truncated to tf32
+// (what the tensor core reads from an fp32 word) and lo = a - hi, exact in
+// fp32; each product is hi*hi + hi*lo + lo*hi, all accumulated in fp32 TMEM.
+// The low parts of M and R are written to global memory once (M by a small
+// kernel, R by GEMM1's epilogue) and loaded by TMA like the high parts; the
+// low part of each X tile is formed in shared memory by the four epilogue
+// warps while the previous stage is multiplied.
+//
+// Operand majors: GEMM1 reads X and M K-major (features contiguous);
+// GEMM2 reads R (targets contiguous) and X (features contiguous) MN-major,
+// so X is never transposed.  Every mbarrier wait is bounded; on expiry the
+// CTA records the failure in a status word, skips its remaining work, frees
+// its TMEM and exits, and the reduction kernel turns the status into NaN.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "glm_common.cuh"
+#include "glm_dense.cuh"
+
+namespace glmb {
+
+namespace {
+
+constexpr int kBM = 128;       // M tile (rows of D / TMEM lanes)
+constexpr int kBN = 256;       // N tile (TMEM columns)
+constexpr int kBK = 32;        // K per stage: one 128-byte swizzle atom of fp32
+constexpr int kStages = 2;
+constexpr int kThreads = 256;  // warp 0: TMA, warp 1: MMA + TMEM, warps 4-7: convert + epilogue
+constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
+constexpr int kBTileBytes = kBN * kBK * 4;  // 32 KB
+constexpr int kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
+constexpr long long kWaitCycles = 4ll << 30;  // ~2 s at 1.9 GHz
+
+enum : int { kGemm1 = 1, kGemm2 = 2 };
+
+struct DenseSmem {
+    // per stage: A (hi), A lo, B (hi), B lo -- each 1024-byte aligned for the swizzle
+    alignas(1024) unsigned char stage[kStages][kStageBytes];
+    unsigned long long full[kStages];   // TMA -> converters
+    unsigned long long ready[kStages];  // converters -> MMA
+    unsigned long long empty[kStages];  // MMA retired -> TMA
+    unsigned long long done;            // all MMAs retired -> epilogue
+    uint32_t tmem_base;
+    int failed;
+};
+
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(saddr(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(unsigned long long* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait: false when the budget ran out (or another role already failed)
+__device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity, volatile int* failed) {
+    const long long t0 = clock64();
+    while (!mbar_test(b, parity)) {
+        if (*failed) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            *failed = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            saddr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(saddr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle.
+// K-major:  rows of 128 B (32 fp32 along K), 8-row groups SBO bytes apart.
+// MN-major: 128 B along M/N (32 fp32), 8 K-rows per 1024-byte atom, atoms
+//           along M/N LBO bytes apart, groups of 8 K-rows SBO bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= uint64_t((addr >> 4) & 0x3FFF);
+    d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+    d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+    d |= uint64_t(1) << 46;  // descriptor version for sm_100
+    d |= uint64_t(2) << 61;  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::tf32: D f32, A/B tf32, majors, N/8, M/16.
+__host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool a_mn_major, bool b_mn_major) {
+    return (1u << 4)                               // D format: f32
+           | (2u << 7)                             // A format: tf32
+           | (2u << 10)                            // B format: tf32
+           | (uint32_t(a_mn_major) << 15)          // A major
+           | (uint32_t(b_mn_major) << 16)          // B major
+           | (uint32_t(N >> 3) << 17)              // N / 8
+           | (uint32_t(M >> 4) << 24);             // M / 16
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(unsigned long long* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_low(float a) {
+    return a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+}
+
+struct DenseArgs {
+    // GEMM1: A = X (K-major, box 32 x 1 x 128), B = M / M_lo (K-major, box 32 x 256 x 1)
+    // GEMM2: A = R / R_lo (MN-major, box 32 x 32 x 1), B = X (MN-major, box 32 x 1 x 32)
+    int64_t nf, nt, ntasks, nobs, nt_pad;
+    int64_t k_begin_step;  // GEMM2: observations per split
+    const float* Y;        // GEMM1 epilogue
+    float* Yhat;           // GEMM1 epilogue (optional)
+    float* R;              // GEMM1 out: [task][obs][nt_pad]
+    float* R_lo;           // GEMM1 out
+    float* P;              // GEMM2 out: [split][task][nt][nf]
+    int* status;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    glm_dense_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapA_lo,
+                          const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapB_lo,
+                          const DenseArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the swizzle needs 1024-byte aligned tiles
+    DenseSmem& sm = *reinterpret_cast<DenseSmem*>(
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023)));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // tile coordinates
+    int64_t m0, n0, task, k0, k1;  // M/N tile origins, K range
+    if constexpr (MODE == kGemm1) {
+        m0 = int64_t(blockIdx.x) * kBM;  // observations
+        n0 = int64_t(blockIdx.y) * kBN;  // targets
+        task = blockIdx.z;
+        k0 = 0;
+        k1 = a.nf;
+    } else {
+        const int64_t ttiles = (a.nt + kBM - 1) / kBM;
+        m0 = int64_t(blockIdx.x % ttiles) * kBM;  // targets
+        n0 = int64_t(blockIdx.x / ttiles) * kBN;  // features
+        const int64_t split = blockIdx.y;
+        task = blockIdx.z;
+        k0 = split * a.k_begin_step;
+        k1 = min(a.nobs, k0 + a.k_begin_step);
+    }
+    const int nkb = int((k1 - k0 + kBK - 1) / kBK);
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.ready[s], 4);  // one arrival per converting warp
+            mbar_init(&sm.empty[s], 1);
+        }
+        mbar_init(&sm.done, 1);
+        sm.failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sm.tmem_base)),
+                     "r"(uint32_t(kBN))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+    volatile int* failed = &sm.failed;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !mbar_wait(&sm.empty[s], uint32_t((kb / kStages - 1) & 1), failed)) break;
+                unsigned char* st = sm.stage[s];
+                unsigned char* A = st;
+                unsigned char* Alo = st + kATileBytes;
+                unsigned char* B = st + 2 * kATileBytes;
+                unsigned char* Blo = st + 2 * kATileBytes + kBTileBytes;
+                const int kk = int(k0 + int64_t(kb) * kBK);
+                if constexpr (MODE == kGemm1) {
+                    mbar_expect_tx(&sm.full[s], kATileBytes + 2 * kBTileBytes);
+                    tma_load_3d(A, &mapA, kk, int(task), int(m0), &sm.full[s]);
+                    tma_load_3d(B, &mapB, kk, int(n0), int(task), &sm.full[s]);
+                    tma_load_3d(Blo, &mapB_lo, kk, int(n0), int(task), &sm.full[s]);
+                } else {
+                    mbar_expect_tx(&sm.full[s], 2 * kATileBytes + kBTileBytes);
+                    // R / R_lo: 4 atoms of 32 targets x 32 observations (4 KB each)
+                    for (int j = 0; j < kBM / 32; ++j) {
+                        tma_load_3d(A + j * 4096, &mapA, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
+                        tma_load_3d(Alo + j * 4096, &mapA_lo, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
+                    }
+                    // X: 8 atoms of 32 features x 32 observations
+                    for (int j = 0; j < kBN / 32; ++j)
+                        tma_load_3d(B + j * 4096, &mapB, int(n0) + 32 * j, int(task), kk, &sm.full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = MODE == kGemm1 ? instr_desc(kBM, kBN, false, false)
+                                                      : instr_desc(kBM, kBN, true, true);
+            bool ok = true;
+            for (int kb = 0; kb < nkb && ok; ++kb) {
+                const int s = kb % kStages;
+                if (!mbar_wait(&sm.ready[s], uint32_t((kb / kStages) & 1), failed)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t base = saddr(sm.stage[s]);
+                const uint32_t A = base, Alo = base + kATileBytes;
+                const uint32_t B = base + 2 * kATileBytes, Blo = B + kBTileBytes;
+#pragma unroll
+                for (int k = 0; k < kBK / 8; ++k) {
+                    uint64_t da, dal, db, dbl;
+                    if constexpr (MODE == kGemm1) {
+                        // K-major: advance 8 fp32 = 32 bytes along the row per MMA
+                        da = smem_desc(A + 32 * k, 16, 1024);
+                        dal = smem_desc(Alo + 32 * k, 16, 1024);
+                        db = smem_desc(B + 32 * k, 16, 1024);
+                        dbl = smem_desc(Blo + 32 * k, 16, 1024);
+                    } else {
+                        // MN-major: advance one 8-row K group (1024 bytes) per MMA
+                        da = smem_desc(A + 1024 * k, 4096, 1024);
+                        dal = smem_desc(Alo + 1024 * k, 4096, 1024);
+                        db = smem_desc(B + 1024 * k, 4096, 1024);
+                        dbl = smem_desc(Blo + 1024 * k, 4096, 1024);
+                    }
+                    const uint32_t acc0 = (kb > 0 || k > 0) ? 1u : 0u;
+                    umma_tf32(tmem, dal, db, idesc, acc0);  // lo * hi
+                    umma_tf32(tmem, da, dbl, idesc, 1u);    // hi * lo
+                    umma_tf32(tmem, da, db, idesc, 1u);     // hi * hi
+                }
+                umma_commit(&sm.empty[s]);
+            }
+            umma_commit(&sm.done);
+        }
+    } else if (warp >= 4) {
+        // ---------------- converters (low parts of X), then epilogue ----------------
+        const int ct = tid - 128;  // 0..127
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int s = kb % kStages;
+            if (!mbar_wait(&sm.full[s], uint32_t((kb / kStages) & 1), failed)) break;
+            unsigned char* st = sm.stage[s];
+            const float4* src = reinterpret_cast<const float4*>(MODE == kGemm1 ? st : st + 2 * kATileBytes);
+            float4* dst = reinterpret_cast<float4*>(MODE == kGemm1 ? st + kATileBytes : st + 2 * kATileBytes + kBTileBytes);
+            const int n4 = (MODE == kGemm1 ? kATileBytes : kBTileBytes) / 16;
+            for (int i = ct; i < n4; i += 128) {
+                const float4 v = src[i];
+                dst[i] = make_float4(tf32_low(v.x), tf32_low(v.y), tf32_low(v.z), tf32_low(v.w));
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.ready[s]);
+        }
+        // epilogue: warp (w-4) reads TMEM lanes [32(w-4), 32(w-4)+32) = rows of D
+        const bool ok = mbar_wait(&sm.done, 0, failed);
+        if (ok) {
+            tc_fence_after();
+            const int row = (warp - 4) * 32 + lane;
+            const uint32_t lane_addr = tmem + (uint32_t((warp - 4) * 32) << 16);
+            if constexpr (MODE == kGemm1) {
+                const int64_t obs = m0 + row;
+                const bool valid_row = obs < a.nobs;
+                for (int c0 = 0; c0 < kBN && n0 + c0 < a.nt; c0 += 32) {
+                    float d[32];
+                    tmem_ld32(lane_addr + uint32_t(c0), d);
+                    if (!valid_row) continue;
+                    const int64_t yrow = (obs * a.ntasks + task) * a.nt;
+                    float* rrow = a.R + (task * a.nobs + obs) * a.nt_pad;
+                    float* rlrow = a.R_lo + (task * a.nobs + obs) * a.nt_pad;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int64_t t = n0 + c0 + i;
+                        if (t < a.nt) {
+                            if (a.Yhat != nullptr) a.Yhat[yrow + t] = d[i];
+                            const float r = d[i] - (a.Y != nullptr ? a.Y[yrow + t] : 0.0f);
+                            rrow[t] = r;
+                            rlrow[t] = tf32_low(r);
+                        }
+                    }
+                }
+            } else {
+                const int64_t t = m0 + row;
+                const bool valid_row = t < a.nt;
+                float* prow = a.P + ((int64_t(blockIdx.y) * a.ntasks + task) * a.nt + t) * a.nf;
+                for (int c0 = 0; c0 < kBN && n0 + c0 < a.nf; c0 += 32) {
+                    float d[32];
+                    tmem_ld32(lane_addr + uint32_t(c0), d);
+                    if (!valid_row) continue;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int64_t f = n0 + c0 + i;
+                        if (f < a.nf) prow[f] = d[i];
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(kBN))
+                     : "memory");
+    }
+    if (tid == 0 && sm.failed) atomicExch(a.status, 1);
+}
+
+__global__ void dense_m_lo_kernel(const float* __restrict__ M, float* __restrict__ M_lo, int64_t n) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        M_lo[i] = tf32_low(M[i]);
+}
+
+// grad[e] (or partial_out[e]) from sum over splits of P[s][e], in double, fixed order.
+__global__ void dense_reduce_kernel(const float* __restrict__ P, int64_t nsplit, int64_t total,
+                                    const float* __restrict__ M, float* __restrict__ grad, double* __restrict__ partial_out,
+                                    double lambda, double alpha, int reg, const int* __restrict__ status) {
+    const bool bad = *status != 0;
+    for (int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+        double s = 0.0;
+        for (int64_t k = 0; k < nsplit; ++k) s += double(P[k * total + e]);
+        if (bad) s = __longlong_as_double(0x7ff8000000000000ll);
+        if (partial_out != nullptr) partial_out[e] = s;
+        else grad[e] = finalize_value<float>(s, M[e], lambda, alpha, reg != 0);
+    }
+}
+
+// ---- tensor maps (driver entry point fetched through the runtime) ----------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D fp32 map: dims (innermost first), byte strides of dims 1 and 2, box.
+bool make_map(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+              const uint32_t box[3]) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool dense_f32_supported(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, const void* X, const void* M) {
+    return nf >= 32 && nf % 4 == 0 && nt >= 1 && ntasks >= 1 && nobs >= 1 && ntasks <= 65535 &&
+           (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && (reinterpret_cast<uintptr_t>(M) & 15u) == 0 &&
+           encode_fn() != nullptr;
+}
+
+DensePlan dense_f32_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
+    DensePlan p;
+    p.nt_pad = (nt + 3) / 4 * 4;
+    const int64_t ttiles = (nt + kBM - 1) / kBM, ftiles = (nf + kBN - 1) / kBN;
+    // observations per GEMM2 split: enough CTAs for a few waves, short fp32 sums
+    const int64_t tiles = std::max<int64_t>(1, ttiles * ftiles * ntasks);
+    int64_t splits = std::max<int64_t>(1, (4 * int64_t(sm_count()) + tiles - 1) / tiles);
+    int64_t per = (nobs + splits - 1) / splits;
+    per = std::min<int64_t>(std::max<int64_t>(per, 4 * kBK), 16384);
+    per = (per + kBK - 1) / kBK * kBK;
+    p.obs_per_split = per;
+    p.nsplit = (nobs + per - 1) / per;
+    const size_t total = size_t(ntasks) * nt * nf;
+    p.r_bytes = round_up(size_t(ntasks) * nobs * p.nt_pad * 4, 256);
+    p.p_bytes = round_up(size_t(p.nsplit) * total * 4, 256);
+    p.mlo_bytes = round_up(total * 4, 256);
+    p.ws_bytes = 2 * p.r_bytes + p.p_bytes + p.mlo_bytes + 256;
+    return p;
+}
+
+int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const float* Y, float* grad,
+                       float* Yhat, double* partial_out, int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,
+                       double lambda, double alpha, bool reg, void* ws, cudaStream_t stream) {
+    char* w = static_cast<char*>(ws);
+    float* R = reinterpret_cast<float*>(w);
+    float* R_lo = reinterpret_cast<float*>(w + p.r_bytes);
+    float* P = reinterpret_cast<float*>(w + 2 * p.r_bytes);
+    float* M_lo = reinterpret_cast<float*>(w + 2 * p.r_bytes + p.p_bytes);
+    int* status = reinterpret_cast<int*>(w + 2 * p.r_bytes + p.p_bytes + p.mlo_bytes);
+    const int64_t total = ntasks * nt * nf;
+    cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return int(e);
+
+    dense_m_lo_kernel<<<unsigned(std::min<int64_t>(4096, (total + 255) / 256)), 256, 0, stream>>>(M, M_lo, total);
+    count_launch();
+
+    CUtensorMap mX1, mM, mMlo, mR, mRlo, mX2;
+    const uint64_t xdims[3] = {uint64_t(nf), uint64_t(ntasks), uint64_t(nobs)};
+    const uint64_t xstr[2] = {uint64_t(nf) * 4, uint64_t(nf * ntasks) * 4};
+    const uint32_t xbox1[3] = {32, 1, kBM}, xbox2[3] = {32, 1, 32};
+    const uint64_t mdims[3] = {uint64_t(nf), uint64_t(nt), uint64_t(ntasks)};
+    const uint64_t mstr[2] = {uint64_t(nf) * 4, uint64_t(nf * nt) * 4};
+    const uint32_t mbox[3] = {32, kBN, 1};
+    const uint64_t rdims[3] = {uint64_t(p.nt_pad), uint64_t(nobs), uint64_t(ntasks)};
+    const uint64_t rstr[2] = {uint64_t(p.nt_pad) * 4, uint64_t(p.nt_pad * nobs) * 4};
+    const uint32_t rbox[3] = {32, 32, 1};
+    if (!make_map(&mX1, X, xdims, xstr, xbox1) || !make_map(&mM, M, mdims, mstr, mbox) ||
+        !make_map(&mMlo, M_lo, mdims, mstr, mbox) || !make_map(&mR, R, rdims, rstr, rbox) ||
+        !make_map(&mRlo, R_lo, rdims, rstr, rbox) || !make_map(&mX2, X, xdims, xstr, xbox2))
+        return GLMB_ERR_UNSUPPORTED;
+
+    const size_t smem = sizeof(DenseSmem) + 1024;
+    static bool attr = false;
+    if (!attr) {
+        if ((e = cudaFuncSetAttribute(glm_dense_gemm_kernel<kGemm1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(smem))) != cudaSuccess)
+            return int(e);
+        if ((e = cudaFuncSetAttribute(glm_dense_gemm_kernel<kGemm2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(smem))) != cudaSuccess)
+            return int(e);
+        attr = true;
+    }
+    DenseArgs args{nf, nt, ntasks, nobs, p.nt_pad, p.obs_per_split, Y, Yhat, R, R_lo, P, status};
+    const dim3 g1(unsigned((nobs + kBM - 1) / kBM), unsigned((nt + kBN - 1) / kBN), unsigned(ntasks));
+    glm_dense_gemm_kernel<kGemm1><<<g1, kThreads, smem, stream>>>(mX1, mX1, mM, mMlo, args);
+    count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    const int64_t ttiles = (nt + kBM - 1) / kBM, ftiles = (nf + kBN - 1) / kBN;
+    const dim3 g2(unsigned(ttiles * ftiles), unsigned(p.nsplit), unsigned(ntasks));
+    glm_dense_gemm_kernel<kGemm2><<<g2, kThreads, smem, stream>>>(mR, mRlo, mX2, mX2, args);
+    count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
+    dense_reduce_kernel<<<unsigned(std::min<int64_t>(4096, (total + 255) / 256)), 256, 0, stream>>>(
+        P, p.nsplit, total, M, grad, partial_out, lambda, alpha, reg ? 1 : 0, status);
+    count_launch();
+    return launch_status();
+}
+
+}  // namespace glmb
