@@ -21,9 +21,11 @@
 //
 // Operand majors: GEMM1 reads X and M K-major (features contiguous);
 // GEMM2 reads R (targets contiguous) and X (features contiguous) MN-major,
-// so X is never transposed.  Every mbarrier wait is bounded; on expiry the
-// CTA records the failure in a status word, skips its remaining work, frees
-// its TMEM and exits, and the reduction kernel turns the status into NaN.
+// so X is never transposed (MN-major 32-bit operands use the 32-byte-chunk
+// variant of the 128-byte swizzle, on both the TMA and the descriptor side).
+// Every mbarrier wait is bounded; on expiry the CTA records the failure in a
+// status word, skips its remaining work, frees its TMEM and exits, and the
+// reduction kernel turns the status into NaN.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -109,17 +111,21 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor (tcgen05 "version 1"), 128-byte swizzle.
-// K-major:  rows of 128 B (32 fp32 along K), 8-row groups SBO bytes apart.
-// MN-major: 128 B along M/N (32 fp32), 8 K-rows per 1024-byte atom, atoms
-//           along M/N LBO bytes apart, groups of 8 K-rows SBO bytes apart.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor (tcgen05 "version 1").
+// K-major (layout 2, 128-byte swizzle of 16-byte chunks): rows of 128 B
+//   (32 fp32 along K), 8-row groups SBO = 1024 bytes apart.
+// MN-major (layout 1, 128-byte swizzle of 32-byte chunks -- the only MN-major
+//   layout the tensor core takes for 32-bit operands): 128 B along M/N
+//   (32 fp32) per K-row, 4-row groups SBO = 512 bytes apart, 32-element
+//   M/N atoms LBO bytes apart.
+constexpr uint32_t kLayoutSW128 = 2, kLayoutSW128Base32B = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
     uint64_t d = 0;
     d |= uint64_t((addr >> 4) & 0x3FFF);
     d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
     d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
     d |= uint64_t(1) << 46;  // descriptor version for sm_100
-    d |= uint64_t(2) << 61;  // SWIZZLE_128B
+    d |= uint64_t(layout & 7) << 61;
     return d;
 }
 
@@ -282,16 +288,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint64_t da, dal, db, dbl;
                     if constexpr (MODE == kGemm1) {
                         // K-major: advance 8 fp32 = 32 bytes along the row per MMA
-                        da = smem_desc(A + 32 * k, 16, 1024);
-                        dal = smem_desc(Alo + 32 * k, 16, 1024);
-                        db = smem_desc(B + 32 * k, 16, 1024);
-                        dbl = smem_desc(Blo + 32 * k, 16, 1024);
+                        da = smem_desc(A + 32 * k, 16, 1024, kLayoutSW128);
+                        dal = smem_desc(Alo + 32 * k, 16, 1024, kLayoutSW128);
+                        db = smem_desc(B + 32 * k, 16, 1024, kLayoutSW128);
+                        dbl = smem_desc(Blo + 32 * k, 16, 1024, kLayoutSW128);
                     } else {
-                        // MN-major: advance one 8-row K group (1024 bytes) per MMA
-                        da = smem_desc(A + 1024 * k, 4096, 1024);
-                        dal = smem_desc(Alo + 1024 * k, 4096, 1024);
-                        db = smem_desc(B + 1024 * k, 4096, 1024);
-                        dbl = smem_desc(Blo + 1024 * k, 4096, 1024);
+                        // MN-major: advance 8 K-rows (two 512-byte groups) per MMA
+                        da = smem_desc(A + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        dal = smem_desc(Alo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        db = smem_desc(B + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        dbl = smem_desc(Blo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
                     }
                     const uint32_t acc0 = (kb > 0 || k > 0) ? 1u : 0u;
                     umma_tf32(tmem, dal, db, idesc, acc0);  // lo * hi
@@ -408,14 +414,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 3-D fp32 map: dims (innermost first), byte strides of dims 1 and 2, box.
+// K-major tiles use the 128-byte swizzle of 16-byte chunks, MN-major tiles
+// the 128-byte swizzle of 32-byte chunks (matching the descriptors above).
 bool make_map(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
-              const uint32_t box[3]) {
+              const uint32_t box[3], bool mn_major) {
     auto fn = encode_fn();
     if (fn == nullptr) return false;
     const cuuint32_t elem_strides[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              CU_TENSOR_MAP_INTERLEAVE_NONE,
+              mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -472,9 +481,9 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
     const uint64_t rdims[3] = {uint64_t(p.nt_pad), uint64_t(nobs), uint64_t(ntasks)};
     const uint64_t rstr[2] = {uint64_t(p.nt_pad) * 4, uint64_t(p.nt_pad * nobs) * 4};
     const uint32_t rbox[3] = {32, 32, 1};
-    if (!make_map(&mX1, X, xdims, xstr, xbox1) || !make_map(&mM, M, mdims, mstr, mbox) ||
-        !make_map(&mMlo, M_lo, mdims, mstr, mbox) || !make_map(&mR, R, rdims, rstr, rbox) ||
-        !make_map(&mRlo, R_lo, rdims, rstr, rbox) || !make_map(&mX2, X, xdims, xstr, xbox2))
+    if (!make_map(&mX1, X, xdims, xstr, xbox1, false) || !make_map(&mM, M, mdims, mstr, mbox, false) ||
+        !make_map(&mMlo, M_lo, mdims, mstr, mbox, false) || !make_map(&mR, R, rdims, rstr, rbox, true) ||
+        !make_map(&mRlo, R_lo, rdims, rstr, rbox, true) || !make_map(&mX2, X, xdims, xstr, xbox2, true))
         return GLMB_ERR_UNSUPPORTED;
 
     const size_t smem = sizeof(DenseSmem) + 1024;

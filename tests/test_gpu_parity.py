@@ -87,6 +87,9 @@ def test_rows_path_is_used_for_hot_shapes():
     assert capi.last_path() == "rows"
     X, M, Y = _inputs(np.float32, 512, 2, 64, 16)
     G.gradient(X, M, Y)
+    assert capi.last_path() == "dense"
+    X, M, Y = _inputs(np.float32, 512, 2, 30, 16)  # features not a multiple of 4
+    G.gradient(X, M, Y)
     assert capi.last_path() == "generic"
 
 
@@ -264,3 +267,32 @@ def test_tiles_path_multitask_f64(oracle):
         assert G.rel_err(g, oracle.gradient(X, M, Y, 0.2, 0.5, True)) <= 1e-11
         g0 = G.gradient(X, M, None, reg=False)
         assert G.rel_err(g0, oracle.gradient(X, M, None, with_reg=False)) <= 1e-11
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 32, 9), (129, 1, 64, 16), (1000, 3, 96, 40), (4097, 1, 256, 256),
+                                   (700, 2, 4096, 12), (3000, 1, 128, 300), (257, 5, 36, 129)])
+def test_dense_path_float32(shape, oracle):
+    """tcgen05 3xTF32 path (many targets): gradient, predictions, partials."""
+    nobs, ntasks, nf, nt = shape
+    X, M, Y = _inputs(np.float32, nobs, ntasks, nf, nt, seed=nobs * 7 + nt)
+    g, yh = G.gradient(X, M, Y, 0.2, 0.3, reg=True, want_yhat=True)
+    assert capi.last_path() == "dense"
+    ref = oracle.gradient_acc64(X, M, Y, 0.2, 0.3, True)
+    assert G.rel_err(g, ref) <= 1e-4
+    assert G.rel_err(g, oracle.gradient(X, M, Y, 0.2, 0.3, True)) <= 1e-4
+    assert G.rel_err(yh, oracle.predict(X.astype(np.float64), M.astype(np.float64))) <= 1e-4
+    assert G.rel_err(G.gradient(X, M, None, reg=False), oracle.gradient_acc64(X, M, None, with_reg=False)) <= 1e-4
+
+
+def test_dense_path_mixed_sign_with_cancellation_floor(oracle):
+    rng = np.random.default_rng(44)
+    nobs, nf, nt = 20000, 512, 64
+    X = (rng.uniform(-1, 1, (nobs, 1, nf)) / np.sqrt(nf)).astype(np.float32)
+    bt = rng.normal(size=(1, nt, nf))
+    Y = (np.einsum("otf,tkf->otk", X.astype(np.float64), bt) + 0.01 * rng.normal(size=(nobs, 1, nt))).astype(np.float32)
+    M = rng.normal(size=(1, nt, nf)).astype(np.float32)  # away from the solution: residuals of order 1
+    g = G.gradient(X, M, Y, 0.001, 0.0, reg=True)
+    assert capi.last_path() == "dense"
+    ref = oracle.gradient_acc64(X, M, Y, 0.001, 0.0, True)
+    assert G.rel_err(g, ref, floor=1e-3 * np.abs(ref).max()) <= 1e-4
+    assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 2e-5
