@@ -16,6 +16,9 @@ Other workloads (--workload):
              CPU-checkable shape (too small to shard: replicas per GPU)
   multitask  64 tasks x 2^18 observations x 256 features x 16 targets,
              float64 (tasks sharded across ranks, no collective)
+  dense      wide dense gradient on the tensor cores (3xTF32): nobs 2^20,
+             nfeatures 4096, ntargets 256, float32, X ~ U(-1,1)/sqrt(4096),
+             lambda2 0.001 (observations sharded)
   fit        elastic-net fit, 20 power iterations + 200 ISTA steps,
              nobs 2^26, nfeatures 512, float32, lambda1 0.05, lambda2 0.01,
              10 %-sparse true coefficients (observations sharded)
@@ -58,7 +61,7 @@ class Workload:
     nt: int
     ntasks: int
     dtype: str  # "f32" | "f64"
-    x: str  # "uniform" (U(-1,1)) | "normal" (N(0,1))
+    x: str  # "uniform" (U(-1,1)) | "normal" (N(0,1)), times x_scale
     noise: float
     shard: str  # "obs" | "tasks" | "replica"
     kind: str = "gradient"  # "gradient" | "fit"
@@ -71,6 +74,7 @@ class Workload:
     n_power: int = 0
     n_iter: int = 0
     block: int = 1 << 16  # rows per seeded generation block
+    x_scale: float = 1.0
 
 
 WORKLOADS = {
@@ -79,6 +83,8 @@ WORKLOADS = {
                        independent_beta=True, block=8192),
     "multitask": Workload("multitask", 1 << 18, 256, 16, 64, "f64", "normal", 0.05, "tasks", lam=0.1,
                           independent_beta=True, block=1 << 14),
+    "dense": Workload("dense", 1 << 20, 4096, 256, 1, "f32", "uniform", 0.01, "obs", lam=0.001,
+                      x_scale=4096 ** -0.5, block=1 << 15),
     "fit": Workload("fit", 1 << 26, 512, 1, 1, "f32", "normal", 0.1, "obs", kind="fit", sparsity=0.1,
                     lambda1=0.05, lambda2=0.01, n_power=20, n_iter=200),
 }
@@ -103,7 +109,7 @@ def parse_args():
     if a.nobs is not None:
         w = Workload(**{**w.__dict__, "nobs": a.nobs, "block": min(w.block, a.nobs)})
     a.w = w
-    default_steps = {"gradient": 500, "driver": 2000, "multitask": 20, "fit": 2}[w.name]
+    default_steps = {"gradient": 500, "driver": 2000, "multitask": 20, "dense": 20, "fit": 2}[w.name]
     a.steps = a.steps if a.steps is not None else default_steps
     a.warmup = a.warmup if a.warmup is not None else (1 if w.kind == "fit" else 10)
     return a
@@ -118,7 +124,8 @@ def workload_config(w: Workload, n_gpus: int, exchange: str = "peer") -> dict:
         "workload": (f"glm_{'fit_elastic_net' if w.kind == 'fit' else 'gradient'} {w.dtype} nobs={w.nobs} "
                      f"nfeatures={w.nf} ntargets={w.nt} ntasks={w.ntasks}"),
         "nobs": w.nobs, "nfeatures": w.nf, "ntargets": w.nt, "ntasks": w.ntasks,
-        "inputs": (f"X~{'U(-1,1)' if w.x == 'uniform' else 'N(0,1)'}, beta~N(0,1)"
+        "inputs": (f"X~{'U(-1,1)' if w.x == 'uniform' else 'N(0,1)'}"
+                   + (f"/sqrt({w.nf})" if w.x_scale != 1.0 else "") + ", beta~N(0,1)"
                    + (f" {int(w.sparsity * 100)}%-sparse" if w.sparsity < 1 else "")
                    + f", y=X beta+N(0,{w.noise}^2), seeded"),
         "l2": "inputs larger than L2 (126 MB), no flush" if w.nobs * w.ntasks * w.nf * 4 > (256 << 20)
@@ -156,6 +163,14 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_bf16_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return None
+
+
 def dram_traffic_per_row(w: Workload):
     """DRAM bytes per observation row of the dominant kernel, from the
     committed ncu summary of that kernel and shape, or None."""
@@ -191,6 +206,7 @@ def cpu_problem(w: Workload, rows: int):
         X = rng.uniform(-1, 1, (rows, w.ntasks, w.nf)).astype(dt)
     else:
         X = rng.normal(size=(rows, w.ntasks, w.nf)).astype(dt)
+    X *= dt(w.x_scale)
     b = rng.normal(size=(w.ntasks, w.nt, w.nf)).astype(dt)
     Y = (np.einsum("otf,tkf->otk", X, b) + w.noise * rng.normal(size=(rows, w.ntasks, w.nt))).astype(dt)
     return X, b, Y
@@ -219,7 +235,8 @@ def cpu_sample_rate(w: Workload, rows: int, reps: int = 3):
 
 
 def cpu_rows(w: Workload) -> int:
-    return min(w.nobs, {"gradient": 1 << 21, "driver": 8192, "multitask": 4096, "fit": 1 << 19}[w.name])
+    return min(w.nobs, {"gradient": 1 << 21, "driver": 8192, "multitask": 4096, "dense": 4096,
+                        "fit": 1 << 19}[w.name])
 
 
 def run_reference(args):
@@ -361,6 +378,8 @@ def make_local(w: Workload, rank: int, world: int, seed: int, device):
                 xs.uniform_(-1.0, 1.0, generator=g)
             else:
                 xs.normal_(generator=g)
+            if w.x_scale != 1.0:
+                xs *= w.x_scale
             noise = torch.randn((rows, w.nt), generator=g, device=device, dtype=dt) * w.noise
             X[b0 - lo:b0 - lo + rows, j, :] = xs
             Y[b0 - lo:b0 - lo + rows, j, :] = xs @ bt.T + noise
@@ -387,6 +406,33 @@ def measured_fp64_tflops(device):
         torch.cuda.synchronize()
         best = min(best, e0.elapsed_time(e1))
     del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def measured_tf32_tflops(device):
+    """cuBLAS TF32 GEMM throughput measured here (the tensor-pipe denominator
+    of the 3xTF32 path; MEASURED_PEAKS.json has bf16 only)."""
+    import torch
+
+    n = 8192
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn((n, n), device=device, dtype=torch.float32)
+        b = torch.randn((n, n), device=device, dtype=torch.float32)
+        torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
     return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
@@ -476,6 +522,7 @@ def run_ours(args):
     step = fit_step if w.kind == "fit" else gradient_step
 
     fp64_peak = measured_fp64_tflops(device) if (w.dtype == "f64" and rank == 0) else None
+    tf32_peak = measured_tf32_tflops(device) if (w.name == "dense" and rank == 0) else None
     props = torch.cuda.get_device_properties(device)
     sampler = ClockSampler(f"GPU-{props.uuid}")
 
@@ -569,8 +616,10 @@ def run_ours(args):
         kernel_name = {"gradient": "glm_rows_kernel (+ finalize): one glmb_gradient call",
                        "driver": "glm_rows_kernel (+ finalize): one glmb_gradient call",
                        "multitask": "glm_tiles_f64_kernel (+ finalize): one glmb_gradient_f64 call",
+                       "dense": "glm_dense_gemm_kernel x2 (GEMM1 residuals, GEMM2 split-K X^T R) + split "
+                                "reduction: one glmb_gradient call",
                        "fit": f"whole fit: {passes} passes of glm_rows_kernel + finalize/prox kernels"}[w.name]
-        if collective and w.kind == "gradient":
+        if collective and w.kind == "gradient" and w.name != "dense":
             kernel_name = ("glm_rows_kernel + glm_exchange_kernel: one glmb_gradient_sharded call"
                            if peer is not None else
                            "glm_rows_kernel (+ partial reduction): one glmb_gradient_partial call")
@@ -580,6 +629,19 @@ def run_ours(args):
             roofline = {"bound": "tensor", "achieved": achieved, "peak": fp64_peak, "unit": "TFLOP/s",
                         "frac": achieved / fp64_peak,
                         "peak_kind": "measured here: cuBLAS DGEMM 8192^3 (FP64; MEASURED_PEAKS.json has none)",
+                        "traffic": None, "algorithmic_flops": flops, "kernel_ms": kernel_ms, "kernel": kernel_name,
+                        "hbm_achieved_gbs": hbm_achieved, "hbm_frac": hbm_achieved / hbm_peak}
+        elif w.name == "dense":
+            # algorithmic fp32 FLOPs (two contractions); the tensor pipe runs 3 tf32 MMAs per product
+            flops = 4.0 * nobs_l * ntasks_l * nf * nt
+            achieved = flops / (kernel_ms * 1e-3) / 1e12
+            peak = tf32_peak / 3.0
+            roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak,
+                        "peak_kind": (f"measured here: cuBLAS TF32 GEMM 8192^3 = {tf32_peak:.1f} TFLOP/s, / 3 for "
+                                      "3xTF32 (MEASURED_PEAKS.json has bf16 only: "
+                                      f"{measured_bf16_peak()} TFLOP/s burst)"),
+                        "tf32_pipe_achieved": 3.0 * achieved, "tf32_peak": tf32_peak,
                         "traffic": None, "algorithmic_flops": flops, "kernel_ms": kernel_ms, "kernel": kernel_name,
                         "hbm_achieved_gbs": hbm_achieved, "hbm_frac": hbm_achieved / hbm_peak}
         else:

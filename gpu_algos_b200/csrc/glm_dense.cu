@@ -11,21 +11,34 @@
 // tcgen05.mma.kind::tf32 with the accumulator in tensor memory (TMEM, 256
 // columns); four warps read TMEM back with tcgen05.ld for the epilogue.
 //
-// 3xTF32 (Ootomo & Yokota, 2022): a = hi + lo with hi = a truncated to tf32
-// (what the tensor core reads from an fp32 word) and lo = a - hi, exact in
-// fp32; each product is hi*hi + hi*lo + lo*hi, all accumulated in fp32 TMEM.
+// 3xTF32 (Ootomo & Yokota, 2022): the tensor core reads the high 19 bits of
+// an fp32 word, i.e. hi = a with its low 13 bits cleared (a tf32 value); the
+// low part a - hi is exact in fp32 and is rounded to the nearest tf32 value
+// (lo, error <= 2^-22 |a|, unbiased).  Each product is hi*hi + hi*lo + lo*hi.
 // The low parts of M and R are written to global memory once (M by a small
-// kernel, R by GEMM1's epilogue) and loaded by TMA like the high parts; the
-// low part of each X tile is formed in shared memory by the four epilogue
+// kernel, R by GEMM1's epilogue) and loaded by TMA next to the fp32 words;
+// the low part of each X tile is formed in shared memory by the epilogue
 // warps while the previous stage is multiplied.
+//
+// Accumulation.  The tensor core rounds each accumulation toward zero, so a
+// long accumulation in TMEM drifts towards zero by about half an ulp of the
+// running sum per MMA: a bias that follows the sign of the result and, where
+// the gradient is a small difference of large terms (near a solution), is far
+// larger than fp32 rounding.  So each 32-deep K block is accumulated from
+// zero in one of two TMEM buffers (256 columns each) -- its 8 small
+// correction products first, then the 4 main ones, so that only 4 roundings
+// happen at the block's full magnitude -- and eight epilogue warps add the
+// block into fp32 registers (round to nearest) while the tensor core fills
+// the other buffer.
 //
 // Operand majors: GEMM1 reads X and M K-major (features contiguous);
 // GEMM2 reads R (targets contiguous) and X (features contiguous) MN-major,
 // so X is never transposed (MN-major 32-bit operands use the 32-byte-chunk
 // variant of the 128-byte swizzle, on both the TMA and the descriptor side).
 // Every mbarrier wait is bounded; on expiry the CTA records the failure in a
-// status word, skips its remaining work, frees its TMEM and exits, and the
-// reduction kernel turns the status into NaN.
+// status word, skips its remaining work, waits (bounded) for its copies and
+// MMAs in flight, frees its TMEM and exits, and the reduction kernel turns
+// the status into NaN.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -40,10 +53,19 @@ namespace glmb {
 namespace {
 
 constexpr int kBM = 128;       // M tile (rows of D / TMEM lanes)
-constexpr int kBN = 256;       // N tile (TMEM columns)
-constexpr int kBK = 32;        // K per stage: one 128-byte swizzle atom of fp32
+constexpr int kBN = 256;       // N tile (columns of one TMEM buffer)
+constexpr int kBK = 32;        // K per stage and per accumulation block: one 128-byte swizzle atom of fp32
 constexpr int kStages = 2;
-constexpr int kThreads = 256;  // warp 0: TMA, warp 1: MMA + TMEM, warps 4-7: convert + epilogue
+constexpr int kEpiWarp0 = 4;   // warps 4..11 (warpgroups 1-2): convert X, drain TMEM, write the tile
+constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter, one per column half
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // warpgroup 0: warp 0 TMA, warp 1 TMEM + MMA
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
+// warpgroup 0 drops to 56 and the two epilogue warpgroups rise to 224, which
+// adds up to the same 64512 (per SM sub-partition: 56 + 224 + 224 = 504 per lane <= 512).
+constexpr uint32_t kRegsControl = 56, kRegsEpilogue = 224;
+static_assert(128 * kRegsControl + 256 * kRegsEpilogue <= kThreads * 168, "register split exceeds the launch");
+constexpr int kColsPerThread = kBN / 2;
+constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulator buffers
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 4;  // 32 KB
 constexpr int kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
@@ -52,12 +74,14 @@ constexpr long long kWaitCycles = 4ll << 30;  // ~2 s at 1.9 GHz
 enum : int { kGemm1 = 1, kGemm2 = 2 };
 
 struct DenseSmem {
-    // per stage: A (hi), A lo, B (hi), B lo -- each 1024-byte aligned for the swizzle
+    // per stage: A, A lo, B, B lo -- each 1024-byte aligned for the swizzle
     alignas(1024) unsigned char stage[kStages][kStageBytes];
     unsigned long long full[kStages];   // TMA -> converters
-    unsigned long long ready[kStages];  // converters -> MMA
-    unsigned long long empty[kStages];  // MMA retired -> TMA
-    unsigned long long done;            // all MMAs retired -> epilogue
+    unsigned long long ready[kStages];  // converters -> MMA (one arrival per epilogue warp)
+    unsigned long long empty[kStages];  // MMAs of the stage retired -> TMA
+    unsigned long long accf[2];         // K block complete in TMEM buffer b -> drainers
+    unsigned long long acce[2];         // TMEM buffer b drained -> MMA (one arrival per epilogue warp)
+    unsigned long long done;            // every MMA retired (teardown)
     uint32_t tmem_base;
     int failed;
 };
@@ -85,13 +109,15 @@ __device__ __forceinline__ bool mbar_test(unsigned long long* b, uint32_t parity
         : "memory");
     return ok != 0;
 }
-// bounded wait: false when the budget ran out (or another role already failed)
+// Bounded wait: false when the budget ran out (which sets *failed) or, with
+// `failed` given, as soon as another role has failed.  Teardown waits pass
+// failed == nullptr and only give up on the budget.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity, volatile int* failed) {
     const long long t0 = clock64();
     while (!mbar_test(b, parity)) {
-        if (*failed) return false;
+        if (failed != nullptr && *failed) return false;
         if (clock64() - t0 > kWaitCycles) {
-            *failed = 1;
+            if (failed != nullptr) *failed = 1;
             return false;
         }
     }
@@ -152,24 +178,44 @@ __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
                  : "memory");
 }
 
-// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ float tf32_low(float a) {
-    return a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+    const float rest = a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(rest));
+    return __uint_as_float(r);
+}
+
+// Adds the K block held in TMEM buffer `buf` (this thread's row, its 128
+// columns) into sum[], then hands the buffer back to the MMA issuer.
+__device__ __forceinline__ bool drain_block(DenseSmem& sm, uint32_t tbase, int blk, float (&sum)[kColsPerThread],
+                                            volatile int* failed) {
+    const int buf = blk & 1;
+    if (!mbar_wait(&sm.accf[buf], uint32_t((blk >> 1) & 1), failed)) return false;
+    tc_fence_after();
+#pragma unroll
+    for (int j = 0; j < kColsPerThread / 16; ++j) {
+        float d[16];
+        tmem_ld16(tbase + uint32_t(buf * kBN + 16 * j), d);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum[16 * j + i] += d[i];
+    }
+    tc_fence_before();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.acce[buf]);
+    return true;
 }
 
 struct DenseArgs {
@@ -179,8 +225,8 @@ struct DenseArgs {
     int64_t k_begin_step;  // GEMM2: observations per split
     const float* Y;        // GEMM1 epilogue
     float* Yhat;           // GEMM1 epilogue (optional)
-    float* R;              // GEMM1 out: [task][obs][nt_pad]
-    float* R_lo;           // GEMM1 out
+    float* R;              // GEMM1 out: Yhat - Y, [task][obs][nt_pad]
+    float* R_lo;           // GEMM1 out: low tf32 part of R
     float* P;              // GEMM2 out: [split][task][nt][nf]
     int* status;
 };
@@ -218,8 +264,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.ready[s], 4);  // one arrival per converting warp
+            mbar_init(&sm.ready[s], kEpiWarps);
             mbar_init(&sm.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sm.accf[b], 1);
+            mbar_init(&sm.acce[b], kEpiWarps);
         }
         mbar_init(&sm.done, 1);
         sm.failed = 0;
@@ -227,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sm.tmem_base)),
-                     "r"(uint32_t(kBN))
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -237,9 +287,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
 
-    if (warp == 0) {
+    if (warp < kEpiWarp0) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+      if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kStages;
                 if (kb >= kStages && !mbar_wait(&sm.empty[s], uint32_t((kb / kStages - 1) & 1), failed)) break;
@@ -265,107 +318,132 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < kBN / 32; ++j)
                         tma_load_3d(B + j * 4096, &mapB, int(n0) + 32 * j, int(task), kk, &sm.full[s]);
                 }
+                issued = kb + 1;
             }
+            // teardown: the copies still in flight land before shared memory is released
+            for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+                mbar_wait(&sm.full[kb % kStages], uint32_t((kb / kStages) & 1), nullptr);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = MODE == kGemm1 ? instr_desc(kBM, kBN, false, false)
                                                       : instr_desc(kBM, kBN, true, true);
-            bool ok = true;
-            for (int kb = 0; kb < nkb && ok; ++kb) {
-                const int s = kb % kStages;
-                if (!mbar_wait(&sm.ready[s], uint32_t((kb / kStages) & 1), failed)) {
-                    ok = false;
-                    break;
-                }
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % kStages, buf = kb & 1;
+                if (kb >= 2 && !mbar_wait(&sm.acce[buf], uint32_t(((kb >> 1) - 1) & 1), failed)) break;
+                if (!mbar_wait(&sm.ready[s], uint32_t((kb / kStages) & 1), failed)) break;
                 tc_fence_after();
                 const uint32_t base = saddr(sm.stage[s]);
                 const uint32_t A = base, Alo = base + kATileBytes;
                 const uint32_t B = base + 2 * kATileBytes, Blo = B + kBTileBytes;
+                const uint32_t d = tmem + uint32_t(buf * kBN);
+                uint64_t da[kBK / 8], dal[kBK / 8], db[kBK / 8], dbl[kBK / 8];
 #pragma unroll
                 for (int k = 0; k < kBK / 8; ++k) {
-                    uint64_t da, dal, db, dbl;
                     if constexpr (MODE == kGemm1) {
                         // K-major: advance 8 fp32 = 32 bytes along the row per MMA
-                        da = smem_desc(A + 32 * k, 16, 1024, kLayoutSW128);
-                        dal = smem_desc(Alo + 32 * k, 16, 1024, kLayoutSW128);
-                        db = smem_desc(B + 32 * k, 16, 1024, kLayoutSW128);
-                        dbl = smem_desc(Blo + 32 * k, 16, 1024, kLayoutSW128);
+                        da[k] = smem_desc(A + 32 * k, 16, 1024, kLayoutSW128);
+                        dal[k] = smem_desc(Alo + 32 * k, 16, 1024, kLayoutSW128);
+                        db[k] = smem_desc(B + 32 * k, 16, 1024, kLayoutSW128);
+                        dbl[k] = smem_desc(Blo + 32 * k, 16, 1024, kLayoutSW128);
                     } else {
                         // MN-major: advance 8 K-rows (two 512-byte groups) per MMA
-                        da = smem_desc(A + 1024 * k, 4096, 512, kLayoutSW128Base32B);
-                        dal = smem_desc(Alo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
-                        db = smem_desc(B + 1024 * k, 4096, 512, kLayoutSW128Base32B);
-                        dbl = smem_desc(Blo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        da[k] = smem_desc(A + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        dal[k] = smem_desc(Alo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        db[k] = smem_desc(B + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        dbl[k] = smem_desc(Blo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
                     }
-                    const uint32_t acc0 = (kb > 0 || k > 0) ? 1u : 0u;
-                    umma_tf32(tmem, dal, db, idesc, acc0);  // lo * hi
-                    umma_tf32(tmem, da, dbl, idesc, 1u);    // hi * lo
-                    umma_tf32(tmem, da, db, idesc, 1u);     // hi * hi
                 }
+                // the block starts from zero: small correction products first, main products last
+#pragma unroll
+                for (int k = 0; k < kBK / 8; ++k) {
+                    umma_tf32(d, dal[k], db[k], idesc, k > 0 ? 1u : 0u);  // lo * hi
+                    umma_tf32(d, da[k], dbl[k], idesc, 1u);               // hi * lo
+                }
+#pragma unroll
+                for (int k = 0; k < kBK / 8; ++k) umma_tf32(d, da[k], db[k], idesc, 1u);  // hi * hi
                 umma_commit(&sm.empty[s]);
+                umma_commit(&sm.accf[buf]);
             }
+            // teardown: every MMA issued has retired before TMEM is freed
             umma_commit(&sm.done);
+            mbar_wait(&sm.done, 0, nullptr);
         }
-    } else if (warp >= 4) {
-        // ---------------- converters (low parts of X), then epilogue ----------------
-        const int ct = tid - 128;  // 0..127
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+        // ---------------- converters (X -> low parts), TMEM drains, epilogue ----------------
+        const int ew = warp - kEpiWarp0;  // 0..7
+        const int quarter = warp & 3;     // the TMEM lanes (rows of D) this warp may read
+        const int half = ew >> 2;         // its 128 columns of D
+        const int ct = tid - kEpiWarp0 * 32;
+        const uint32_t tbase = tmem + (uint32_t(32 * quarter) << 16) + uint32_t(half * kColsPerThread);
+        float sum[kColsPerThread];
+#pragma unroll
+        for (int i = 0; i < kColsPerThread; ++i) sum[i] = 0.0f;
+        bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
             const int s = kb % kStages;
-            if (!mbar_wait(&sm.full[s], uint32_t((kb / kStages) & 1), failed)) break;
+            if (!mbar_wait(&sm.full[s], uint32_t((kb / kStages) & 1), failed)) {
+                ok = false;
+                break;
+            }
             unsigned char* st = sm.stage[s];
             const float4* src = reinterpret_cast<const float4*>(MODE == kGemm1 ? st : st + 2 * kATileBytes);
             float4* dst = reinterpret_cast<float4*>(MODE == kGemm1 ? st + kATileBytes : st + 2 * kATileBytes + kBTileBytes);
-            const int n4 = (MODE == kGemm1 ? kATileBytes : kBTileBytes) / 16;
-            for (int i = ct; i < n4; i += 128) {
+            constexpr int n4 = (MODE == kGemm1 ? kATileBytes : kBTileBytes) / 16;
+#pragma unroll 4
+            for (int i = ct; i < n4; i += kEpiWarps * 32) {
                 const float4 v = src[i];
                 dst[i] = make_float4(tf32_low(v.x), tf32_low(v.y), tf32_low(v.z), tf32_low(v.w));
             }
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.ready[s]);
+            // the previous block is (nearly) done by now: fold it in while this one is multiplied
+            if (kb >= 1 && !drain_block(sm, tbase, kb - 1, sum, failed)) {
+                ok = false;
+                break;
+            }
         }
-        // epilogue: warp (w-4) reads TMEM lanes [32(w-4), 32(w-4)+32) = rows of D
-        const bool ok = mbar_wait(&sm.done, 0, failed);
-        if (ok) {
-            tc_fence_after();
-            const int row = (warp - 4) * 32 + lane;
-            const uint32_t lane_addr = tmem + (uint32_t((warp - 4) * 32) << 16);
-            if constexpr (MODE == kGemm1) {
-                const int64_t obs = m0 + row;
-                const bool valid_row = obs < a.nobs;
-                for (int c0 = 0; c0 < kBN && n0 + c0 < a.nt; c0 += 32) {
-                    float d[32];
-                    tmem_ld32(lane_addr + uint32_t(c0), d);
-                    if (!valid_row) continue;
-                    const int64_t yrow = (obs * a.ntasks + task) * a.nt;
-                    float* rrow = a.R + (task * a.nobs + obs) * a.nt_pad;
-                    float* rlrow = a.R_lo + (task * a.nobs + obs) * a.nt_pad;
+        if (ok && nkb >= 1) ok = drain_block(sm, tbase, nkb - 1, sum, failed);
+
+        const int row = 32 * quarter + lane;
+        const int64_t c0 = n0 + int64_t(half) * kColsPerThread;
+        if constexpr (MODE == kGemm1) {
+            const int64_t obs = m0 + row;
+            if (ok && obs < a.nobs) {
+                // columns [nt, nt_pad) hold zeros (M is zero-filled there) and are written as such
+                const int64_t yrow = (obs * a.ntasks + task) * a.nt;
+                float* rrow = a.R + (task * a.nobs + obs) * a.nt_pad;
+                float* rlrow = a.R_lo + (task * a.nobs + obs) * a.nt_pad;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int64_t t = n0 + c0 + i;
-                        if (t < a.nt) {
-                            if (a.Yhat != nullptr) a.Yhat[yrow + t] = d[i];
-                            const float r = d[i] - (a.Y != nullptr ? a.Y[yrow + t] : 0.0f);
-                            rrow[t] = r;
-                            rlrow[t] = tf32_low(r);
+                for (int i = 0; i < kColsPerThread; i += 4) {
+                    const int64_t t = c0 + i;
+                    if (t < a.nt_pad) {
+                        float r[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const bool in = t + u < a.nt;
+                            if (in && a.Yhat != nullptr) a.Yhat[yrow + t + u] = sum[i + u];
+                            r[u] = sum[i + u] - (in && a.Y != nullptr ? a.Y[yrow + t + u] : 0.0f);
                         }
+                        *reinterpret_cast<float4*>(rrow + t) = make_float4(r[0], r[1], r[2], r[3]);
+                        *reinterpret_cast<float4*>(rlrow + t) =
+                            make_float4(tf32_low(r[0]), tf32_low(r[1]), tf32_low(r[2]), tf32_low(r[3]));
                     }
                 }
-            } else {
-                const int64_t t = m0 + row;
-                const bool valid_row = t < a.nt;
+            }
+        } else {
+            const int64_t t = m0 + row;
+            if (ok && t < a.nt) {
                 float* prow = a.P + ((int64_t(blockIdx.y) * a.ntasks + task) * a.nt + t) * a.nf;
-                for (int c0 = 0; c0 < kBN && n0 + c0 < a.nf; c0 += 32) {
-                    float d[32];
-                    tmem_ld32(lane_addr + uint32_t(c0), d);
-                    if (!valid_row) continue;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int64_t f = n0 + c0 + i;
-                        if (f < a.nf) prow[f] = d[i];
-                    }
+                for (int i = 0; i < kColsPerThread; i += 4) {
+                    const int64_t f = c0 + i;
+                    if (f < a.nf)  // nf is a multiple of 4
+                        *reinterpret_cast<float4*>(prow + f) = make_float4(sum[i], sum[i + 1], sum[i + 2], sum[i + 3]);
                 }
             }
         }
@@ -374,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(kBN))
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                      : "memory");
     }
     if (tid == 0 && sm.failed) atomicExch(a.status, 1);

@@ -284,15 +284,35 @@ def test_dense_path_float32(shape, oracle):
     assert G.rel_err(G.gradient(X, M, None, reg=False), oracle.gradient_acc64(X, M, None, with_reg=False)) <= 1e-4
 
 
-def test_dense_path_mixed_sign_with_cancellation_floor(oracle):
-    rng = np.random.default_rng(44)
-    nobs, nf, nt = 20000, 512, 64
+def _dense_problem(nobs, nf, nt, at_solution, seed=44):
+    """Config-4-like data: X ~ U(-1,1)/sqrt(nf), Y = X beta + N(0, 0.01^2);
+    the gradient is taken at beta itself (residuals are the noise: a small
+    difference of large terms) or at an independent N(0,1) draw."""
+    rng = np.random.default_rng(seed)
     X = (rng.uniform(-1, 1, (nobs, 1, nf)) / np.sqrt(nf)).astype(np.float32)
     bt = rng.normal(size=(1, nt, nf))
     Y = (np.einsum("otf,tkf->otk", X.astype(np.float64), bt) + 0.01 * rng.normal(size=(nobs, 1, nt))).astype(np.float32)
-    M = rng.normal(size=(1, nt, nf)).astype(np.float32)  # away from the solution: residuals of order 1
+    M = (bt if at_solution else rng.normal(size=(1, nt, nf))).astype(np.float32)
+    return X, M, Y
+
+
+def test_dense_path_mixed_sign_with_cancellation_floor(oracle):
+    X, M, Y = _dense_problem(20000, 512, 64, at_solution=False)
     g = G.gradient(X, M, Y, 0.001, 0.0, reg=True)
     assert capi.last_path() == "dense"
     ref = oracle.gradient_acc64(X, M, Y, 0.001, 0.0, True)
     assert G.rel_err(g, ref, floor=1e-3 * np.abs(ref).max()) <= 1e-4
-    assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 2e-5
+    assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 2e-6
+
+
+def test_dense_path_at_the_solution(oracle):
+    """Residuals of order 0.01 against predictions of order 0.6: the tensor
+    core's round-toward-zero accumulation is bounded by the per-block drains;
+    the result stays within 1e-4 of the exact gradient in norm (the fp32
+    host algorithm: about 1e-5)."""
+    X, M, Y = _dense_problem(20000, 512, 64, at_solution=True)
+    g = G.gradient(X, M, Y, 0.001, 0.0, reg=True)
+    assert capi.last_path() == "dense"
+    ref = oracle.gradient_acc64(X, M, Y, 0.001, 0.0, True)
+    assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 1e-4
+    assert np.abs(g - ref).max() <= 2e-4 * np.abs(ref).max()
