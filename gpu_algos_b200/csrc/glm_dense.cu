@@ -5,11 +5,11 @@
 //   GEMM1  R[obs, t] = sum_f X[obs, f] M[t, f] - Y[obs, t]      (K = features)
 //   GEMM2  P_s[t, f] = sum_{obs in split s} R[obs, t] X[obs, f]  (K = observations)
 // followed by a fixed-order double sum over the splits s and the elastic-net
-// finalize.  Both GEMMs run glm_dense_gemm_kernel: TMA (cp.async.bulk.tensor,
-// 128-byte swizzle) stages 128 x 32 and 256 x 32 fp32 tiles into shared
-// memory through a two-stage mbarrier ring; one thread issues
-// tcgen05.mma.kind::tf32 with the accumulator in tensor memory (TMEM, 256
-// columns); four warps read TMEM back with tcgen05.ld for the epilogue.
+// finalize.  Both GEMMs run glm_dense_gemm_kernel (a 128 x 256 output tile
+// per CTA): TMA (cp.async.bulk.tensor, swizzled) stages 128 x 32 and 256 x 32
+// fp32 tiles (and the low parts of M and R) into shared memory through a
+// two-stage mbarrier ring; one thread issues tcgen05.mma.kind::tf32 with the
+// accumulators in tensor memory (TMEM).
 //
 // 3xTF32 (Ootomo & Yokota, 2022): the tensor core reads the high 19 bits of
 // an fp32 word, i.e. hi = a with its low 13 bits cleared (a tf32 value); the
@@ -31,10 +31,11 @@
 // block into fp32 registers (round to nearest) while the tensor core fills
 // the other buffer.
 //
-// Operand majors: GEMM1 reads X and M K-major (features contiguous);
-// GEMM2 reads R (targets contiguous) and X (features contiguous) MN-major,
-// so X is never transposed (MN-major 32-bit operands use the 32-byte-chunk
-// variant of the 128-byte swizzle, on both the TMA and the descriptor side).
+// Operand majors: GEMM1 reads X and M K-major (features contiguous, 128-byte
+// swizzle: one 32-float row per K block); GEMM2 reads R (targets contiguous)
+// and X (features contiguous) MN-major, so X is never transposed (MN-major
+// 32-bit operands use the 32-byte-chunk variant of the 128-byte swizzle, on
+// both the TMA and the descriptor side).
 // Every mbarrier wait is bounded; on expiry the CTA records the failure in a
 // status word, skips its remaining work, waits (bounded) for its copies and
 // MMAs in flight, frees its TMEM and exits, and the reduction kernel turns
@@ -54,7 +55,7 @@ namespace {
 
 constexpr int kBM = 128;       // M tile (rows of D / TMEM lanes)
 constexpr int kBN = 256;       // N tile (columns of one TMEM buffer)
-constexpr int kBK = 32;        // K per stage and per accumulation block: one 128-byte swizzle atom of fp32
+constexpr int kBK = 32;        // K per stage and per accumulation block (128 bytes of fp32)
 constexpr int kStages = 2;
 constexpr int kEpiWarp0 = 4;   // warps 4..11 (warpgroups 1-2): convert X, drain TMEM, write the tile
 constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter, one per column half
@@ -68,6 +69,7 @@ constexpr int kColsPerThread = kBN / 2;
 constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulator buffers
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
 constexpr int kBTileBytes = kBN * kBK * 4;  // 32 KB
+constexpr int kAtomBytes = 32 * kBK * 4;    // MN-major: 32 M/N elements x kBK K-rows
 constexpr int kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
 constexpr long long kWaitCycles = 4ll << 30;  // ~2 s at 1.9 GHz
 
@@ -138,13 +140,17 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // Shared-memory matrix descriptor (tcgen05 "version 1").
-// K-major (layout 2, 128-byte swizzle of 16-byte chunks): rows of 128 B
-//   (32 fp32 along K), 8-row groups SBO = 1024 bytes apart.
+// K-major: one row of kBK fp32 per M/N element -- the 64-byte swizzle
+//   (layout 4) for kBK = 16, the 128-byte one (layout 2) for kBK = 32 --
+//   8-row groups SBO = 8 rows apart.
 // MN-major (layout 1, 128-byte swizzle of 32-byte chunks -- the only MN-major
 //   layout the tensor core takes for 32-bit operands): 128 B along M/N
 //   (32 fp32) per K-row, 4-row groups SBO = 512 bytes apart, 32-element
 //   M/N atoms LBO bytes apart.
-constexpr uint32_t kLayoutSW128 = 2, kLayoutSW128Base32B = 1;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+constexpr uint32_t kLayoutKMajor = kBK == 32 ? 2u : 4u;
+constexpr uint32_t kSboKMajor = 8 * kBK * 4;
+static_assert(kBK == 16 || kBK == 32, "K block: one 64- or 128-byte swizzle row");
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
     uint64_t d = 0;
     d |= uint64_t((addr >> 4) & 0x3FFF);
@@ -178,17 +184,31 @@ __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
                  : "memory");
 }
 
-// 16 consecutive fp32 columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes; the values
+// are valid after tmem_wait_ld.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Waits for this thread's outstanding TMEM loads.  The registers pass through
+// the statement so that no use of them is scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+// Orders later uses of r after the preceding volatile statement (a wait).
+__device__ __forceinline__ void reg_after(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]));
 }
 
 __device__ __forceinline__ float tf32_low(float a) {
@@ -205,12 +225,20 @@ __device__ __forceinline__ bool drain_block(DenseSmem& sm, uint32_t tbase, int b
     const int buf = blk & 1;
     if (!mbar_wait(&sm.accf[buf], uint32_t((blk >> 1) & 1), failed)) return false;
     tc_fence_after();
+    // two batches of 64 columns: four loads in flight per wait
 #pragma unroll
-    for (int j = 0; j < kColsPerThread / 16; ++j) {
-        float d[16];
-        tmem_ld16(tbase + uint32_t(buf * kBN + 16 * j), d);
+    for (int hb = 0; hb < kColsPerThread / 64; ++hb) {
+        uint32_t r[4][16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sum[16 * j + i] += d[i];
+        for (int j = 0; j < 4; ++j) tmem_ld16(tbase + uint32_t(buf * kBN + 64 * hb + 16 * j), r[j]);
+        tmem_wait_ld(r[0]);
+        reg_after(r[1]);
+        reg_after(r[2]);
+        reg_after(r[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[64 * hb + 16 * j + i] += __uint_as_float(r[j][i]);
     }
     tc_fence_before();
     __syncwarp();
@@ -219,8 +247,8 @@ __device__ __forceinline__ bool drain_block(DenseSmem& sm, uint32_t tbase, int b
 }
 
 struct DenseArgs {
-    // GEMM1: A = X (K-major, box 32 x 1 x 128), B = M / M_lo (K-major, box 32 x 256 x 1)
-    // GEMM2: A = R / R_lo (MN-major, box 32 x 32 x 1), B = X (MN-major, box 32 x 1 x 32)
+    // GEMM1: A = X (K-major, box 16 x 1 x 128), B = M / M_lo (K-major, box 16 x 256 x 1)
+    // GEMM2: A = R / R_lo (MN-major, box 32 x 16 x 1), B = X (MN-major, box 32 x 1 x 16)
     int64_t nf, nt, ntasks, nobs, nt_pad;
     int64_t k_begin_step;  // GEMM2: observations per split
     const float* Y;        // GEMM1 epilogue
@@ -292,6 +320,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
+            // Every GEMM1 CTA reads all of M: CTAs start at different K blocks
+            // so that they do not all ask the same L2 lines for the same tile
+            // at once (measured: GEMM1 8% faster; GEMM2, whose shared R tiles
+            // are read by 16 CTAs, was slower with it).  The drains sum whole
+            // blocks, in this CTA's own fixed order.
+            const int rot =
+                MODE == kGemm1 && nkb > 1 ? int((blockIdx.x * 37u + blockIdx.y * 11u) % unsigned(nkb)) : 0;
             int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kStages;
@@ -301,7 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 unsigned char* Alo = st + kATileBytes;
                 unsigned char* B = st + 2 * kATileBytes;
                 unsigned char* Blo = st + 2 * kATileBytes + kBTileBytes;
-                const int kk = int(k0 + int64_t(kb) * kBK);
+                const int kr = kb + rot < nkb ? kb + rot : kb + rot - nkb;
+                const int kk = int(k0 + int64_t(kr) * kBK);
                 if constexpr (MODE == kGemm1) {
                     mbar_expect_tx(&sm.full[s], kATileBytes + 2 * kBTileBytes);
                     tma_load_3d(A, &mapA, kk, int(task), int(m0), &sm.full[s]);
@@ -309,14 +345,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_3d(Blo, &mapB_lo, kk, int(n0), int(task), &sm.full[s]);
                 } else {
                     mbar_expect_tx(&sm.full[s], 2 * kATileBytes + kBTileBytes);
-                    // R / R_lo: 4 atoms of 32 targets x 32 observations (4 KB each)
+                    // R / R_lo: 4 atoms of 32 targets x kBK observations
                     for (int j = 0; j < kBM / 32; ++j) {
-                        tma_load_3d(A + j * 4096, &mapA, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
-                        tma_load_3d(Alo + j * 4096, &mapA_lo, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
+                        tma_load_3d(A + j * kAtomBytes, &mapA, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
+                        tma_load_3d(Alo + j * kAtomBytes, &mapA_lo, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
                     }
-                    // X: 8 atoms of 32 features x 32 observations
+                    // X: 8 atoms of 32 features x kBK observations
                     for (int j = 0; j < kBN / 32; ++j)
-                        tma_load_3d(B + j * 4096, &mapB, int(n0) + 32 * j, int(task), kk, &sm.full[s]);
+                        tma_load_3d(B + j * kAtomBytes, &mapB, int(n0) + 32 * j, int(task), kk, &sm.full[s]);
                 }
                 issued = kb + 1;
             }
@@ -343,16 +379,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < kBK / 8; ++k) {
                     if constexpr (MODE == kGemm1) {
                         // K-major: advance 8 fp32 = 32 bytes along the row per MMA
-                        da[k] = smem_desc(A + 32 * k, 16, 1024, kLayoutSW128);
-                        dal[k] = smem_desc(Alo + 32 * k, 16, 1024, kLayoutSW128);
-                        db[k] = smem_desc(B + 32 * k, 16, 1024, kLayoutSW128);
-                        dbl[k] = smem_desc(Blo + 32 * k, 16, 1024, kLayoutSW128);
+                        da[k] = smem_desc(A + 32 * k, 16, kSboKMajor, kLayoutKMajor);
+                        dal[k] = smem_desc(Alo + 32 * k, 16, kSboKMajor, kLayoutKMajor);
+                        db[k] = smem_desc(B + 32 * k, 16, kSboKMajor, kLayoutKMajor);
+                        dbl[k] = smem_desc(Blo + 32 * k, 16, kSboKMajor, kLayoutKMajor);
                     } else {
                         // MN-major: advance 8 K-rows (two 512-byte groups) per MMA
-                        da[k] = smem_desc(A + 1024 * k, 4096, 512, kLayoutSW128Base32B);
-                        dal[k] = smem_desc(Alo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
-                        db[k] = smem_desc(B + 1024 * k, 4096, 512, kLayoutSW128Base32B);
-                        dbl[k] = smem_desc(Blo + 1024 * k, 4096, 512, kLayoutSW128Base32B);
+                        da[k] = smem_desc(A + 1024 * k, kAtomBytes, 512, kLayoutSW128Base32B);
+                        dal[k] = smem_desc(Alo + 1024 * k, kAtomBytes, 512, kLayoutSW128Base32B);
+                        db[k] = smem_desc(B + 1024 * k, kAtomBytes, 512, kLayoutSW128Base32B);
+                        dbl[k] = smem_desc(Blo + 1024 * k, kAtomBytes, 512, kLayoutSW128Base32B);
                     }
                 }
                 // the block starts from zero: small correction products first, main products last
@@ -492,8 +528,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 3-D fp32 map: dims (innermost first), byte strides of dims 1 and 2, box.
-// K-major tiles use the 128-byte swizzle of 16-byte chunks, MN-major tiles
-// the 128-byte swizzle of 32-byte chunks (matching the descriptors above).
+// K-major tiles use the 64- or 128-byte swizzle (one row per kBK floats),
+// MN-major tiles the 128-byte swizzle of 32-byte chunks (matching the
+// descriptors above).
 bool make_map(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
               const uint32_t box[3], bool mn_major) {
     auto fn = encode_fn();
@@ -501,7 +538,8 @@ bool make_map(CUtensorMap* map, const void* base, const uint64_t dims[3], const 
     const cuuint32_t elem_strides[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
               CU_TENSOR_MAP_INTERLEAVE_NONE,
-              mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+              mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                       : (kBK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B),
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -552,13 +590,13 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
     CUtensorMap mX1, mM, mMlo, mR, mRlo, mX2;
     const uint64_t xdims[3] = {uint64_t(nf), uint64_t(ntasks), uint64_t(nobs)};
     const uint64_t xstr[2] = {uint64_t(nf) * 4, uint64_t(nf * ntasks) * 4};
-    const uint32_t xbox1[3] = {32, 1, kBM}, xbox2[3] = {32, 1, 32};
+    const uint32_t xbox1[3] = {kBK, 1, kBM}, xbox2[3] = {32, 1, kBK};
     const uint64_t mdims[3] = {uint64_t(nf), uint64_t(nt), uint64_t(ntasks)};
     const uint64_t mstr[2] = {uint64_t(nf) * 4, uint64_t(nf * nt) * 4};
-    const uint32_t mbox[3] = {32, kBN, 1};
+    const uint32_t mbox[3] = {kBK, kBN, 1};
     const uint64_t rdims[3] = {uint64_t(p.nt_pad), uint64_t(nobs), uint64_t(ntasks)};
     const uint64_t rstr[2] = {uint64_t(p.nt_pad) * 4, uint64_t(p.nt_pad * nobs) * 4};
-    const uint32_t rbox[3] = {32, 32, 1};
+    const uint32_t rbox[3] = {32, kBK, 1};
     if (!make_map(&mX1, X, xdims, xstr, xbox1, false) || !make_map(&mM, M, mdims, mstr, mbox, false) ||
         !make_map(&mMlo, M_lo, mdims, mstr, mbox, false) || !make_map(&mR, R, rdims, rstr, rbox, true) ||
         !make_map(&mRlo, R_lo, rdims, rstr, rbox, true) || !make_map(&mX2, X, xdims, xstr, xbox2, true))
