@@ -5,11 +5,16 @@
 //   GEMM1  R[obs, t] = sum_f X[obs, f] M[t, f] - Y[obs, t]      (K = features)
 //   GEMM2  P_s[t, f] = sum_{obs in split s} R[obs, t] X[obs, f]  (K = observations)
 // followed by a fixed-order double sum over the splits s and the elastic-net
-// finalize.  Both GEMMs run glm_dense_gemm_kernel (a 128 x 256 output tile
-// per CTA): TMA (cp.async.bulk.tensor, swizzled) stages 128 x 32 and 256 x 32
-// fp32 tiles (and the low parts of M and R) into shared memory through a
-// two-stage mbarrier ring; one thread issues tcgen05.mma.kind::tf32 with the
-// accumulators in tensor memory (TMEM).
+// finalize.  Both GEMMs run glm_dense_gemm_kernel on CTA pairs (a cluster of
+// two CTAs on two SMs) that compute a 256 x 256 output tile together with
+// tcgen05.mma.cta_group::2: each CTA stages its own 128 rows of A and its own
+// 128 columns of B (with their low parts) into its shared memory -- TMA
+// (cp.async.bulk.tensor, swizzled), a three-stage mbarrier ring of 64 KB
+// stages -- and holds its 128 rows of the result in its tensor memory (TMEM);
+// one thread of the even CTA issues the MMAs for the pair.  Splitting B over
+// the pair halves the bytes each SM must bring in per MMA, which pays for
+// the deeper ring: with one CTA per tile, two 96 KB stages could not hide
+// the L2 latency of the next K block behind the MMAs of the current one.
 //
 // 3xTF32 (Ootomo & Yokota, 2022): the tensor core reads the high 19 bits of
 // an fp32 word, i.e. hi = a with its low 13 bits cleared (a tf32 value); the
@@ -36,10 +41,15 @@
 // and X (features contiguous) MN-major, so X is never transposed (MN-major
 // 32-bit operands use the 32-byte-chunk variant of the 128-byte swizzle, on
 // both the TMA and the descriptor side).
+// Pair protocol: each CTA waits for its own TMA copies; its converter warps
+// then arrive on the even CTA's `ready` barrier (remote arrive, cluster
+// scope), and its drain warps on the even CTA's `acce` barrier; the MMA
+// issuer's commits reach both CTAs' `empty`, `accf` and `done` barriers
+// (tcgen05.commit multicast).  No TMA copy is multicast.
 // Every mbarrier wait is bounded; on expiry the CTA records the failure in a
 // status word, skips its remaining work, waits (bounded) for its copies and
-// MMAs in flight, frees its TMEM and exits, and the reduction kernel turns
-// the status into NaN.
+// MMAs in flight, meets its peer at the final cluster barrier, frees its
+// TMEM and exits, and the reduction kernel turns the status into NaN.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -53,37 +63,44 @@ namespace glmb {
 
 namespace {
 
-constexpr int kBM = 128;       // M tile (rows of D / TMEM lanes)
-constexpr int kBN = 256;       // N tile (columns of one TMEM buffer)
+constexpr int kBM = 128;       // rows of D per CTA (TMEM lanes); a pair covers 256
+constexpr int kBN = 256;       // columns of D (of one TMEM buffer), shared by the pair
+constexpr int kBNHalf = kBN / 2;  // columns of B staged by each CTA
 constexpr int kBK = 32;        // K per stage and per accumulation block (128 bytes of fp32)
-constexpr int kStages = 2;
-constexpr int kEpiWarp0 = 4;   // warps 4..11 (warpgroups 1-2): convert X, drain TMEM, write the tile
+constexpr int kStages = 3;
+// Warp roles (16 warps): warp 0 TMA, warp 1 TMEM + MMA issue, warps 2-3 and
+// 12-15 form the low parts of the staged X tiles, warps 4-11 (warpgroups 1-2)
+// drain TMEM and write the tile -- conversion and drains run side by side.
+constexpr int kEpiWarp0 = 4;   // first drain warp
 constexpr int kEpiWarps = 8;   // two warps per TMEM lane quarter, one per column half
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // warpgroup 0: warp 0 TMA, warp 1 TMEM + MMA
-// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64512);
-// warpgroup 0 drops to 56 and the two epilogue warpgroups rise to 224, which
-// adds up to the same 64512 (per SM sub-partition: 56 + 224 + 224 = 504 per lane <= 512).
-constexpr uint32_t kRegsControl = 56, kRegsEpilogue = 224;
-static_assert(128 * kRegsControl + 256 * kRegsEpilogue <= kThreads * 168, "register split exceeds the launch");
+constexpr int kConvWarps = 6;
+constexpr int kThreads = 16 * 32;
+// Register split (setmaxnreg): launched at 128 per thread (512 x 128 = 65536);
+// warpgroups 0 and 3 drop to 56 and the two drain warpgroups rise to 200,
+// which adds up to the same 65536 (per SM sub-partition: 56 + 200 + 200 + 56 = 512 per lane).
+constexpr uint32_t kRegsControl = 56, kRegsEpilogue = 200;
+static_assert(256 * kRegsControl + 256 * kRegsEpilogue <= kThreads * 128, "register split exceeds the launch");
 constexpr int kColsPerThread = kBN / 2;
 constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulator buffers
 constexpr int kATileBytes = kBM * kBK * 4;  // 16 KB
-constexpr int kBTileBytes = kBN * kBK * 4;  // 32 KB
+constexpr int kBTileBytes = kBNHalf * kBK * 4;  // 16 KB
 constexpr int kAtomBytes = 32 * kBK * 4;    // MN-major: 32 M/N elements x kBK K-rows
 constexpr int kStageBytes = 2 * kATileBytes + 2 * kBTileBytes;
 constexpr long long kWaitCycles = 4ll << 30;  // ~2 s at 1.9 GHz
+constexpr uint32_t kReadyArrivals = 2 * kConvWarps;  // converter warps of both CTAs
+constexpr uint32_t kDrainArrivals = 2 * kEpiWarps;   // drain warps of both CTAs
 
 enum : int { kGemm1 = 1, kGemm2 = 2 };
 
 struct DenseSmem {
     // per stage: A, A lo, B, B lo -- each 1024-byte aligned for the swizzle
     alignas(1024) unsigned char stage[kStages][kStageBytes];
-    unsigned long long full[kStages];   // TMA -> converters
-    unsigned long long ready[kStages];  // converters -> MMA (one arrival per epilogue warp)
-    unsigned long long empty[kStages];  // MMAs of the stage retired -> TMA
-    unsigned long long accf[2];         // K block complete in TMEM buffer b -> drainers
-    unsigned long long acce[2];         // TMEM buffer b drained -> MMA (one arrival per epilogue warp)
-    unsigned long long done;            // every MMA retired (teardown)
+    unsigned long long full[kStages];   // this CTA's TMA -> its converters
+    unsigned long long ready[kStages];  // (even CTA) converters of both CTAs -> MMA
+    unsigned long long empty[kStages];  // MMAs of the stage retired -> each CTA's TMA
+    unsigned long long accf[2];         // K block complete in TMEM buffer b -> each CTA's drainers
+    unsigned long long acce[2];         // (even CTA) buffer b drained in both CTAs -> MMA
+    unsigned long long done;            // every MMA of the pair retired (teardown)
     uint32_t tmem_base;
     int failed;
 };
@@ -99,9 +116,6 @@ __device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, uint32_t b
                  "r"(bytes)
                  : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(saddr(b)) : "memory");
-}
 __device__ __forceinline__ bool mbar_test(unsigned long long* b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -110,6 +124,26 @@ __device__ __forceinline__ bool mbar_test(unsigned long long* b, uint32_t parity
         : "r"(saddr(b)), "r"(parity)
         : "memory");
     return ok != 0;
+}
+// Arrive on the barrier at the same shared-memory offset in CTA `rank` of
+// this cluster (default semantics: release at CTA scope).  What the arrival
+// publishes is either tensor-core input in this CTA's shared memory, made
+// visible to the async proxy by fence.proxy.async beforehand, or the end of
+// this CTA's TMEM reads, ordered by tcgen05.fence::before_thread_sync.
+// (A release at cluster scope measured 750-1200 cycles per arrival here.)
+__device__ __forceinline__ void mbar_arrive_rank(unsigned long long* b, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr(b)), "r"(rank));
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Both CTAs of the pair reach this point (every thread of both).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Bounded wait: false when the budget ran out (which sets *failed) or, with
 // `failed` given, as soon as another role has failed.  Teardown waits pass
@@ -172,16 +206,24 @@ __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool a_mn_major,
            | (uint32_t(M >> 4) << 24);             // M / 16
 }
 
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+// D[256 x N] (+)= A[256 x 8] B[8 x N] over the pair: rows 0-127 of A and D
+// in the even CTA, rows 128-255 in the odd one, B's N columns split in halves
+// the same way; descriptors and the TMEM address are offsets valid in both.
+__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                               uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void umma_commit(unsigned long long* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
-                 : "memory");
+// One arrival on `bar` in both CTAs of the pair once the MMAs issued so far retire.
+__device__ __forceinline__ void umma_commit_pair(unsigned long long* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            saddr(bar)),
+        "h"(uint16_t(3))
+        : "memory");
 }
 
 // 16 consecutive 32-bit columns of this warp's 32 TMEM lanes; the values
@@ -225,30 +267,29 @@ __device__ __forceinline__ bool drain_block(DenseSmem& sm, uint32_t tbase, int b
     const int buf = blk & 1;
     if (!mbar_wait(&sm.accf[buf], uint32_t((blk >> 1) & 1), failed)) return false;
     tc_fence_after();
-    // two batches of 64 columns: four loads in flight per wait
+    // batches of 32 columns: two loads in flight per wait
 #pragma unroll
-    for (int hb = 0; hb < kColsPerThread / 64; ++hb) {
-        uint32_t r[4][16];
+    for (int hb = 0; hb < kColsPerThread / 32; ++hb) {
+        uint32_t r[2][16];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) tmem_ld16(tbase + uint32_t(buf * kBN + 64 * hb + 16 * j), r[j]);
+        for (int j = 0; j < 2; ++j) tmem_ld16(tbase + uint32_t(buf * kBN + 32 * hb + 16 * j), r[j]);
         tmem_wait_ld(r[0]);
         reg_after(r[1]);
-        reg_after(r[2]);
-        reg_after(r[3]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sum[64 * hb + 16 * j + i] += __uint_as_float(r[j][i]);
+            for (int i = 0; i < 16; ++i) sum[32 * hb + 16 * j + i] += __uint_as_float(r[j][i]);
     }
     tc_fence_before();
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.acce[buf]);
+    if ((threadIdx.x & 31) == 0) mbar_arrive_rank(&sm.acce[buf], 0);
     return true;
 }
 
 struct DenseArgs {
-    // GEMM1: A = X (K-major, box 16 x 1 x 128), B = M / M_lo (K-major, box 16 x 256 x 1)
-    // GEMM2: A = R / R_lo (MN-major, box 32 x 16 x 1), B = X (MN-major, box 32 x 1 x 16)
+    // Per CTA of a pair:
+    // GEMM1: A = X (K-major, box kBK x 1 x 128), B = M / M_lo (K-major, box kBK x 128 x 1)
+    // GEMM2: A = R / R_lo (MN-major, box 32 x kBK x 1), B = X (MN-major, box 32 x 1 x kBK)
     int64_t nf, nt, ntasks, nobs, nt_pad;
     int64_t k_begin_step;  // GEMM2: observations per split
     const float* Y;        // GEMM1 epilogue
@@ -260,73 +301,79 @@ struct DenseArgs {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     glm_dense_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapA_lo,
                           const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapB_lo,
                           const DenseArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // the swizzle needs 1024-byte aligned tiles
+    // the swizzle needs 1024-byte aligned tiles (same offsets in both CTAs of the pair)
     DenseSmem& sm = *reinterpret_cast<DenseSmem*>(
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023)));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();  // 0: even CTA (issues the MMAs), 1: odd CTA
+    const int64_t pair = blockIdx.x >> 1;
 
-    // tile coordinates
-    int64_t m0, n0, task, k0, k1;  // M/N tile origins, K range
+    // tile coordinates: m0 = this CTA's 128 rows of D (and of A), n0 = the
+    // pair's 256 columns of D, nb0 = the 128 columns of B this CTA stages
+    int64_t m0, n0, task, k0, k1;
     if constexpr (MODE == kGemm1) {
-        m0 = int64_t(blockIdx.x) * kBM;  // observations
-        n0 = int64_t(blockIdx.y) * kBN;  // targets
+        m0 = pair * (2 * kBM) + int64_t(rank) * kBM;  // observations
+        n0 = int64_t(blockIdx.y) * kBN;               // targets
         task = blockIdx.z;
         k0 = 0;
         k1 = a.nf;
     } else {
-        const int64_t ttiles = (a.nt + kBM - 1) / kBM;
-        m0 = int64_t(blockIdx.x % ttiles) * kBM;  // targets
-        n0 = int64_t(blockIdx.x / ttiles) * kBN;  // features
+        const int64_t ttiles = (a.nt + 2 * kBM - 1) / (2 * kBM);
+        m0 = (pair % ttiles) * (2 * kBM) + int64_t(rank) * kBM;  // targets
+        n0 = (pair / ttiles) * kBN;                               // features
         const int64_t split = blockIdx.y;
         task = blockIdx.z;
         k0 = split * a.k_begin_step;
         k1 = min(a.nobs, k0 + a.k_begin_step);
     }
+    const int64_t nb0 = n0 + int64_t(rank) * kBNHalf;
     const int nkb = int((k1 - k0 + kBK - 1) / kBK);
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.ready[s], kEpiWarps);
+            mbar_init(&sm.ready[s], kReadyArrivals);
             mbar_init(&sm.empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sm.accf[b], 1);
-            mbar_init(&sm.acce[b], kEpiWarps);
+            mbar_init(&sm.acce[b], kDrainArrivals);
         }
         mbar_init(&sm.done, 1);
         sm.failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sm.tmem_base)),
+        // both CTAs allocate, with the same warp and the same destination offset
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&sm.tmem_base)),
                      "r"(kTmemCols)
                      : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // the peer's barriers exist before anyone arrives on them
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
     volatile int* failed = &sm.failed;
 
-    if (warp < kEpiWarp0) {
+    if (warp < kEpiWarp0 || warp >= kEpiWarp0 + kEpiWarps) {
       asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
       if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (each CTA: its A rows, its half of B) ----------------
         if (lane == 0) {
-            // Every GEMM1 CTA reads all of M: CTAs start at different K blocks
+            // Every GEMM1 pair reads all of M: pairs start at different K blocks
             // so that they do not all ask the same L2 lines for the same tile
             // at once (measured: GEMM1 8% faster; GEMM2, whose shared R tiles
-            // are read by 16 CTAs, was slower with it).  The drains sum whole
-            // blocks, in this CTA's own fixed order.
+            // are read by many pairs, was slower with it).  Both CTAs of a pair
+            // use the same order; the drains sum whole blocks in that order.
             const int rot =
-                MODE == kGemm1 && nkb > 1 ? int((blockIdx.x * 37u + blockIdx.y * 11u) % unsigned(nkb)) : 0;
+                MODE == kGemm1 && nkb > 1 ? int((unsigned(pair) * 37u + blockIdx.y * 11u) % unsigned(nkb)) : 0;
             int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kStages;
@@ -341,8 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (MODE == kGemm1) {
                     mbar_expect_tx(&sm.full[s], kATileBytes + 2 * kBTileBytes);
                     tma_load_3d(A, &mapA, kk, int(task), int(m0), &sm.full[s]);
-                    tma_load_3d(B, &mapB, kk, int(n0), int(task), &sm.full[s]);
-                    tma_load_3d(Blo, &mapB_lo, kk, int(n0), int(task), &sm.full[s]);
+                    tma_load_3d(B, &mapB, kk, int(nb0), int(task), &sm.full[s]);
+                    tma_load_3d(Blo, &mapB_lo, kk, int(nb0), int(task), &sm.full[s]);
                 } else {
                     mbar_expect_tx(&sm.full[s], 2 * kATileBytes + kBTileBytes);
                     // R / R_lo: 4 atoms of 32 targets x kBK observations
@@ -350,9 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_3d(A + j * kAtomBytes, &mapA, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
                         tma_load_3d(Alo + j * kAtomBytes, &mapA_lo, int(m0) + 32 * j, kk, int(task), &sm.full[s]);
                     }
-                    // X: 8 atoms of 32 features x kBK observations
-                    for (int j = 0; j < kBN / 32; ++j)
-                        tma_load_3d(B + j * kAtomBytes, &mapB, int(n0) + 32 * j, int(task), kk, &sm.full[s]);
+                    // X: 4 atoms of 32 features x kBK observations
+                    for (int j = 0; j < kBNHalf / 32; ++j)
+                        tma_load_3d(B + j * kAtomBytes, &mapB, int(nb0) + 32 * j, int(task), kk, &sm.full[s]);
                 }
                 issued = kb + 1;
             }
@@ -360,11 +407,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
                 mbar_wait(&sm.full[kb % kStages], uint32_t((kb / kStages) & 1), nullptr);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = MODE == kGemm1 ? instr_desc(kBM, kBN, false, false)
-                                                      : instr_desc(kBM, kBN, true, true);
+      } else if (warp == 1 && lane == 0) {
+        if (rank == 0) {
+            // ---------------- MMA issuer (even CTA, for the pair) ----------------
+            constexpr uint32_t idesc = MODE == kGemm1 ? instr_desc(2 * kBM, kBN, false, false)
+                                                      : instr_desc(2 * kBM, kBN, true, true);
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % kStages, buf = kb & 1;
                 if (kb >= 2 && !mbar_wait(&sm.acce[buf], uint32_t(((kb >> 1) - 1) & 1), failed)) break;
@@ -394,56 +441,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // the block starts from zero: small correction products first, main products last
 #pragma unroll
                 for (int k = 0; k < kBK / 8; ++k) {
-                    umma_tf32(d, dal[k], db[k], idesc, k > 0 ? 1u : 0u);  // lo * hi
-                    umma_tf32(d, da[k], dbl[k], idesc, 1u);               // hi * lo
+                    umma_tf32_pair(d, dal[k], db[k], idesc, k > 0 ? 1u : 0u);  // lo * hi
+                    umma_tf32_pair(d, da[k], dbl[k], idesc, 1u);               // hi * lo
                 }
 #pragma unroll
-                for (int k = 0; k < kBK / 8; ++k) umma_tf32(d, da[k], db[k], idesc, 1u);  // hi * hi
-                umma_commit(&sm.empty[s]);
-                umma_commit(&sm.accf[buf]);
+                for (int k = 0; k < kBK / 8; ++k) umma_tf32_pair(d, da[k], db[k], idesc, 1u);  // hi * hi
+                umma_commit_pair(&sm.empty[s]);
+                umma_commit_pair(&sm.accf[buf]);
             }
-            // teardown: every MMA issued has retired before TMEM is freed
-            umma_commit(&sm.done);
-            mbar_wait(&sm.done, 0, nullptr);
+            // teardown: every MMA issued has retired (in both CTAs) before TMEM is freed
+            umma_commit_pair(&sm.done);
         }
-      }
-    } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
-        // ---------------- converters (X -> low parts), TMEM drains, epilogue ----------------
-        const int ew = warp - kEpiWarp0;  // 0..7
-        const int quarter = warp & 3;     // the TMEM lanes (rows of D) this warp may read
-        const int half = ew >> 2;         // its 128 columns of D
-        const int ct = tid - kEpiWarp0 * 32;
-        const uint32_t tbase = tmem + (uint32_t(32 * quarter) << 16) + uint32_t(half * kColsPerThread);
-        float sum[kColsPerThread];
-#pragma unroll
-        for (int i = 0; i < kColsPerThread; ++i) sum[i] = 0.0f;
-        bool ok = true;
+        mbar_wait(&sm.done, 0, nullptr);
+      } else if (warp >= 2) {
+        // ---------------- converters: low parts of the staged X tiles ----------------
+        const int ct = (warp < kEpiWarp0 ? warp - 2 : warp - (kEpiWarp0 + kEpiWarps) + 2) * 32 + lane;
         for (int kb = 0; kb < nkb; ++kb) {
             const int s = kb % kStages;
-            if (!mbar_wait(&sm.full[s], uint32_t((kb / kStages) & 1), failed)) {
-                ok = false;
-                break;
-            }
+            if (!mbar_wait(&sm.full[s], uint32_t((kb / kStages) & 1), failed)) break;
             unsigned char* st = sm.stage[s];
             const float4* src = reinterpret_cast<const float4*>(MODE == kGemm1 ? st : st + 2 * kATileBytes);
-            float4* dst = reinterpret_cast<float4*>(MODE == kGemm1 ? st + kATileBytes : st + 2 * kATileBytes + kBTileBytes);
+            float4* dst =
+                reinterpret_cast<float4*>(MODE == kGemm1 ? st + kATileBytes : st + 2 * kATileBytes + kBTileBytes);
             constexpr int n4 = (MODE == kGemm1 ? kATileBytes : kBTileBytes) / 16;
-#pragma unroll 4
-            for (int i = ct; i < n4; i += kEpiWarps * 32) {
+#pragma unroll 2
+            for (int i = ct; i < n4; i += kConvWarps * 32) {
                 const float4 v = src[i];
                 dst[i] = make_float4(tf32_low(v.x), tf32_low(v.y), tf32_low(v.z), tf32_low(v.w));
             }
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.ready[s]);
-            // the previous block is (nearly) done by now: fold it in while this one is multiplied
-            if (kb >= 1 && !drain_block(sm, tbase, kb - 1, sum, failed)) {
-                ok = false;
-                break;
-            }
+            if (lane == 0) mbar_arrive_rank(&sm.ready[s], 0);
         }
-        if (ok && nkb >= 1) ok = drain_block(sm, tbase, nkb - 1, sum, failed);
+      }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+        // ---------------- TMEM drains, then the tile's epilogue ----------------
+        const int ew = warp - kEpiWarp0;  // 0..7
+        const int quarter = warp & 3;     // the TMEM lanes (rows of D) this warp may read
+        const int half = ew >> 2;         // its 128 columns of D
+        const uint32_t tbase = tmem + (uint32_t(32 * quarter) << 16) + uint32_t(half * kColsPerThread);
+        float sum[kColsPerThread];
+#pragma unroll
+        for (int i = 0; i < kColsPerThread; ++i) sum[i] = 0.0f;
+        bool ok = true;
+        for (int kb = 0; kb < nkb && ok; ++kb) ok = drain_block(sm, tbase, kb, sum, failed);
 
         const int row = 32 * quarter + lane;
         const int64_t c0 = n0 + int64_t(half) * kColsPerThread;
@@ -486,9 +528,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // no arrival or MMA operand read targets a CTA that has left
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                      : "memory");
     }
     if (tid == 0 && sm.failed) atomicExch(a.status, 1);
@@ -554,10 +597,10 @@ bool dense_f32_supported(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, c
 DensePlan dense_f32_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
     DensePlan p;
     p.nt_pad = (nt + 3) / 4 * 4;
-    const int64_t ttiles = (nt + kBM - 1) / kBM, ftiles = (nf + kBN - 1) / kBN;
-    // observations per GEMM2 split: enough CTAs for a few waves, short fp32 sums
-    const int64_t tiles = std::max<int64_t>(1, ttiles * ftiles * ntasks);
-    int64_t splits = std::max<int64_t>(1, (4 * int64_t(sm_count()) + tiles - 1) / tiles);
+    const int64_t ttiles = (nt + 2 * kBM - 1) / (2 * kBM), ftiles = (nf + kBN - 1) / kBN;
+    // observations per GEMM2 split: enough CTAs (two per 256 x 256 tile) for a few waves
+    const int64_t ctas = std::max<int64_t>(1, 2 * ttiles * ftiles * ntasks);
+    int64_t splits = std::max<int64_t>(1, (4 * int64_t(sm_count()) + ctas - 1) / ctas);
     int64_t per = (nobs + splits - 1) / splits;
     per = std::min<int64_t>(std::max<int64_t>(per, 4 * kBK), 16384);
     per = (per + kBK - 1) / kBK * kBK;
@@ -593,7 +636,7 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
     const uint32_t xbox1[3] = {kBK, 1, kBM}, xbox2[3] = {32, 1, kBK};
     const uint64_t mdims[3] = {uint64_t(nf), uint64_t(nt), uint64_t(ntasks)};
     const uint64_t mstr[2] = {uint64_t(nf) * 4, uint64_t(nf * nt) * 4};
-    const uint32_t mbox[3] = {kBK, kBN, 1};
+    const uint32_t mbox[3] = {kBK, kBNHalf, 1};
     const uint64_t rdims[3] = {uint64_t(p.nt_pad), uint64_t(nobs), uint64_t(ntasks)};
     const uint64_t rstr[2] = {uint64_t(p.nt_pad) * 4, uint64_t(p.nt_pad * nobs) * 4};
     const uint32_t rbox[3] = {32, kBK, 1};
@@ -614,12 +657,13 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
         attr = true;
     }
     DenseArgs args{nf, nt, ntasks, nobs, p.nt_pad, p.obs_per_split, Y, Yhat, R, R_lo, P, status};
-    const dim3 g1(unsigned((nobs + kBM - 1) / kBM), unsigned((nt + kBN - 1) / kBN), unsigned(ntasks));
+    // grids count CTAs: two per pair (the kernel's cluster shape)
+    const dim3 g1(unsigned(2 * ((nobs + 2 * kBM - 1) / (2 * kBM))), unsigned((nt + kBN - 1) / kBN), unsigned(ntasks));
     glm_dense_gemm_kernel<kGemm1><<<g1, kThreads, smem, stream>>>(mX1, mX1, mM, mMlo, args);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
-    const int64_t ttiles = (nt + kBM - 1) / kBM, ftiles = (nf + kBN - 1) / kBN;
-    const dim3 g2(unsigned(ttiles * ftiles), unsigned(p.nsplit), unsigned(ntasks));
+    const int64_t ttiles = (nt + 2 * kBM - 1) / (2 * kBM), ftiles = (nf + kBN - 1) / kBN;
+    const dim3 g2(unsigned(2 * ttiles * ftiles), unsigned(p.nsplit), unsigned(ntasks));
     glm_dense_gemm_kernel<kGemm2><<<g2, kThreads, smem, stream>>>(mR, mRlo, mX2, mX2, args);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return int(e);
