@@ -172,15 +172,16 @@ def measured_bf16_peak():
 
 
 def dram_traffic_per_row(w: Workload):
-    """DRAM bytes per observation row of the dominant kernel, from the
+    """DRAM bytes per observation row of the measured call, from the
     committed ncu summary of that kernel and shape, or None."""
-    name = {"gradient": "glm_rows_f32_nf128_traffic.txt"}.get(w.name)
+    name = {"gradient": "glm_rows_f32_nf128_traffic.txt",
+            "dense": "glm_dense_f32_nf4096_nt256_traffic.txt"}.get(w.name)
     if name is None:
         return None
     try:
         with open(os.path.join(REPO, "profiles", name)) as f:
             for line in f:
-                if line.startswith("dram_bytes_per_row:"):
+                if line.startswith(("dram_bytes_per_row:", "dram_bytes_per_obs:")):
                     return float(line.split(":", 1)[1])
     except OSError:
         pass
@@ -616,8 +617,8 @@ def run_ours(args):
         kernel_name = {"gradient": "glm_rows_kernel (+ finalize): one glmb_gradient call",
                        "driver": "glm_rows_kernel (+ finalize): one glmb_gradient call",
                        "multitask": "glm_tiles_f64_kernel (+ finalize): one glmb_gradient_f64 call",
-                       "dense": "glm_dense_gemm_kernel x2 (GEMM1 residuals, GEMM2 split-K X^T R) + split "
-                                "reduction: one glmb_gradient call",
+                       "dense": "glm_dense_gemm_kernel x2 on CTA pairs (GEMM1 residuals, GEMM2 split-K X^T R) "
+                                "+ split reduction: one glmb_gradient call",
                        "fit": f"whole fit: {passes} passes of glm_rows_kernel + finalize/prox kernels"}[w.name]
         if collective and w.kind == "gradient" and w.name != "dense":
             kernel_name = ("glm_rows_kernel + glm_exchange_kernel: one glmb_gradient_sharded call"
@@ -642,7 +643,7 @@ def run_ours(args):
                                       "3xTF32 (MEASURED_PEAKS.json has bf16 only: "
                                       f"{measured_bf16_peak()} TFLOP/s burst)"),
                         "tf32_pipe_achieved": 3.0 * achieved, "tf32_peak": tf32_peak,
-                        "traffic": None, "algorithmic_flops": flops, "kernel_ms": kernel_ms, "kernel": kernel_name,
+                        "traffic": (tpr * nobs_l) if tpr is not None else None, "algorithmic_flops": flops, "kernel_ms": kernel_ms, "kernel": kernel_name,
                         "hbm_achieved_gbs": hbm_achieved, "hbm_frac": hbm_achieved / hbm_peak}
         else:
             roofline = {"bound": "hbm", "achieved": hbm_achieved, "peak": hbm_peak, "unit": "GB/s",
