@@ -51,7 +51,11 @@ namespace {
 
 constexpr int kExThreads = 256;
 constexpr int kExMaxBlocks = 64;     // flags per sender
-constexpr int kExElemsPerBlock = 64;  // target chunk (one warp per element, 8 warps)
+// Target chunk: one element per warp.  The first phase (the fixed-order sum of
+// a rank's CTA partials, as glm_finalize_kernel does it) is bound by L2
+// latency, so elements are spread over warps, not walked by one (8 elements
+// per warp cost 30 us per call where one costs 4).
+constexpr int kExElemsPerBlock = kExThreads / 32;
 
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -97,6 +101,8 @@ __global__ void __launch_bounds__(kExThreads)
     // 1. this rank's partial for the block's elements: fixed-order sum of the CTA partials
     for (int64_t e = lo + warp; e < hi; e += nwarps) {
         double s = 0.0;
+        // unrolled: eight independent loads in flight, the additions in the same order
+#pragma unroll 8
         for (int64_t c = lane; c < a.nparts; c += 32) s += a.part[e * a.nparts + c];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);

@@ -181,6 +181,16 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
 
         // step 2: yhat for an 8 x 8 (rows x targets) block per warp
         if (g1_nt * 8 < nt) {
+            const int row = g1_mt * 8 + (lane >> 2);
+            const int64_t obs = base + row;
+            // this lane's two y values, loaded before the contraction so that
+            // their global-memory latency hides behind it
+            double yv[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int t = g1_nt * 8 + (lane & 3) * 2 + i;
+                yv[i] = (a.Y != nullptr && obs < obs_end && t < nt) ? a.Y[(obs * ntasks + task) * a.nt + t] : 0.0;
+            }
             // four independent accumulator chains over k (k0 mod 16) keep the
             // tensor pipe busy instead of waiting on one dependent chain
             double dk[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
@@ -197,16 +207,13 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
             double d[2];
 #pragma unroll
             for (int i = 0; i < 2; ++i) d[i] = (dk[0][i] + dk[1][i]) + (dk[2][i] + dk[3][i]);
-            const int row = g1_mt * 8 + (lane >> 2);
-            const int64_t obs = base + row;
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int t = g1_nt * 8 + (lane & 3) * 2 + i;
                 double r = 0.0;
                 if (obs < obs_end && t < nt) {
-                    const int64_t yi = (obs * ntasks + task) * a.nt + t;
-                    if (a.Yhat != nullptr) a.Yhat[yi] = d[i];
-                    r = d[i] - (a.Y != nullptr ? a.Y[yi] : 0.0);
+                    if (a.Yhat != nullptr) a.Yhat[(obs * ntasks + task) * a.nt + t] = d[i];
+                    r = d[i] - yv[i];
                 }
                 sm.R[row][t] = r;
             }
