@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(256)
     const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
     for (int64_t e = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; e < total; e += nwarps) {
         P s = P(0);
+        // unrolled: eight independent loads in flight, the additions in the same order
+#pragma unroll 8
         for (int64_t c = lane; c < nparts; c += kWarp) s += part[e * nparts + c];
 #pragma unroll
         for (int off = kWarp / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
