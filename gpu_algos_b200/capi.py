@@ -64,6 +64,9 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"glmb_gradient_{s}")
         f.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P, _SZ, _P]
         f.restype = _INT
+        f = getattr(L, f"glmb_loss_{s}")
+        f.argtypes = [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _P, _SZ, _P]
+        f.restype = _INT
     for s in FLOATING:
         sig = {
             "glmb_gradient_partial": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _U32, _P, _SZ, _P],
@@ -74,6 +77,7 @@ def _declare(L: ctypes.CDLL) -> None:
             "glmb_power_init": [_P, _I64, _I64, _U64, _P],
             "glmb_fit_elastic_net": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _INT, _INT,
                                      _U64, _P, _SZ, _P],
+            "glmb_gradient_loss": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P, _SZ, _P],
         }
         for name, args in sig.items():
             f = getattr(L, f"{name}_{s}")
@@ -145,11 +149,12 @@ def exported_symbols() -> list[str]:
     """Every entry point declared in include/glm_b200.h (for the load test)."""
     names = ["glmb_version", "glmb_status_string", "glmb_launch_count", "glmb_last_path"]
     for s in SUFFIXES:
-        names += [f"glmb_predict_{s}", f"glmb_gradient_workspace_size_{s}", f"glmb_gradient_{s}"]
+        names += [f"glmb_predict_{s}", f"glmb_gradient_workspace_size_{s}", f"glmb_gradient_{s}",
+                  f"glmb_loss_{s}"]
     for s in FLOATING:
         names += [f"glmb_gradient_partial_{s}", f"glmb_gradient_finalize_{s}", f"glmb_prox_step_{s}",
                   f"glmb_prox_update_{s}", f"glmb_power_step_{s}", f"glmb_power_init_{s}",
-                  f"glmb_fit_workspace_size_{s}", f"glmb_fit_elastic_net_{s}"]
+                  f"glmb_fit_workspace_size_{s}", f"glmb_fit_elastic_net_{s}", f"glmb_gradient_loss_{s}"]
     names.append("glmb_gradient_noalloc_f32")
     names += ["glmb_peer_group_create", "glmb_peer_group_connect", "glmb_peer_group_connect_local",
               "glmb_peer_group_buffer", "glmb_peer_group_status", "glmb_peer_group_destroy"]

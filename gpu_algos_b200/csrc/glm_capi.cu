@@ -22,6 +22,7 @@
 
 #include "glm_common.cuh"
 #include "glm_dense.cuh"
+#include "glm_loss.cuh"
 #include "glm_fit.cuh"
 #include "glm_generic.cuh"
 #include "glm_peer.cuh"
@@ -135,7 +136,8 @@ size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
         }
     }
     if (!all_rows) need = std::max(need, generic_workspace_bytes<T>(nf, nt, ntasks, nobs));
-    return need;
+    // glmb_gradient_loss_* reuses the workspace for the loss after the gradient
+    return std::max(need, loss_workspace_bytes());
 }
 
 // Shared body of glmb_gradient_* (partial_out == NULL) and
@@ -377,6 +379,19 @@ const char* glmb_last_path(void) { return glmb::g_last_path; }
                 reinterpret_cast<NT_*>(Yhat), nullptr, nf, nt, ntasks, nobs, lambda, alpha, flags, \
                 workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));               \
         });                                                                                        \
+    }                                                                                              \
+    int glmb_loss_##SFX(const CT* M, const CT* Y, const CT* Yhat, CT* loss, int64_t nf, int64_t nt, \
+                        int64_t ntasks, int64_t nobs, double lambda, double alpha, void* workspace, \
+                        size_t workspace_bytes, glmb_stream_t stream) {                            \
+        if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0) return GLMB_ERR_INVALID_VALUE;             \
+        return guarded([&] {                                                                       \
+            const int st = glmb::check_device();                                                   \
+            if (st != GLMB_OK) return st;                                                          \
+            return glmb::loss_launch<NT_>(                                                         \
+                reinterpret_cast<const NT_*>(M), reinterpret_cast<const NT_*>(Y),                  \
+                reinterpret_cast<const NT_*>(Yhat), reinterpret_cast<NT_*>(loss), nf, nt, ntasks,  \
+                nobs, lambda, alpha, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream)); \
+        });                                                                                        \
     }
 
 GLMB_DEFINE_BASIC(f16, uint16_t, __half)
@@ -392,6 +407,22 @@ GLMB_DEFINE_BASIC(u32, uint32_t, uint32_t)
 GLMB_DEFINE_BASIC(u64, uint64_t, uint64_t)
 
 #define GLMB_DEFINE_FLOATING(SFX, T)                                                               \
+    int glmb_gradient_loss_##SFX(const T* X, const T* M, const T* Y, T* grad_M, T* Yhat, T* loss,  \
+                                 int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,             \
+                                 double lambda, double alpha, uint32_t flags, void* workspace,     \
+                                 size_t workspace_bytes, glmb_stream_t stream) {                   \
+        if (loss == nullptr || (Yhat == nullptr && nobs * nt * ntasks > 0)) return GLMB_ERR_INVALID_VALUE; \
+        return guarded([&] {                                                                       \
+            const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);                         \
+            int st = glmb::gradient_impl<T>(X, M, Y, grad_M, Yhat, nullptr, nf, nt, ntasks, nobs,  \
+                                            lambda, alpha, flags | GLMB_GRAD_WRITE_YHAT, workspace, \
+                                            workspace_bytes, s);                                   \
+            if (st != GLMB_OK) return st;                                                          \
+            /* the gradient's scratch is free again in stream order */                             \
+            return glmb::loss_launch<T>(M, (flags & GLMB_GRAD_Y_ZERO) ? nullptr : Y, Yhat, loss, nf, nt, \
+                                        ntasks, nobs, lambda, alpha, workspace, workspace_bytes, s); \
+        });                                                                                        \
+    }                                                                                              \
     int glmb_gradient_partial_##SFX(const T* X, const T* M, const T* Y, double* partial, T* Yhat, \
                                     int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,          \
                                     uint32_t flags, void* workspace, size_t workspace_bytes,       \

@@ -106,6 +106,49 @@ def gradient(X, M, Y, lam: float = 0.0, alpha: float = 0.0, regularize: bool = T
     return out
 
 
+def loss(M, Y, Yhat, lam: float = 0.0, alpha: float = 0.0, out=None, workspace=None, stream=None):
+    """sum (Yhat - Y)^2 + lam * (alpha * sum|M| + (1 - alpha) * sum M^2), as a
+    one-element tensor of M's dtype (``Y=None``: zeros)."""
+    sfx = SUFFIX[M.dtype]
+    ntasks, nt, nf = M.shape
+    nobs = Yhat.shape[0]
+    _need(Yhat, "Yhat", (nobs, ntasks, nt), M.dtype)
+    if Y is not None:
+        _need(Y, "Y", (nobs, ntasks, nt), M.dtype)
+    if out is None:
+        out = torch.empty((1,), dtype=M.dtype, device=M.device)
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    capi.call(f"glmb_loss_{sfx}", _ptr(M), _ptr(Y), _ptr(Yhat), _ptr(out), nf, nt, ntasks, nobs,
+              float(lam), float(alpha), ws_ptr, ws_bytes, _stream(stream))
+    return out
+
+
+def gradient_loss(X, M, Y, lam: float = 0.0, alpha: float = 0.0, regularize: bool = True,
+                  yhat_out=None, out=None, loss_out=None, workspace=None, stream=None):
+    """Gradient (as :func:`gradient`) and loss (as :func:`loss`, always with
+    the elastic-net term) from one call; returns (grad, loss, yhat)."""
+    sfx = SUFFIX[X.dtype]
+    nf, nt, ntasks, nobs = _dims(X, M)
+    _need(X, "X", (nobs, ntasks, nf), X.dtype)
+    _need(M, "M", (ntasks, nt, nf), X.dtype)
+    flags = capi.GRAD_REGULARIZE if regularize else 0
+    if Y is None:
+        flags |= capi.GRAD_Y_ZERO
+    else:
+        _need(Y, "Y", (nobs, ntasks, nt), X.dtype)
+    if yhat_out is None:
+        yhat_out = torch.empty((nobs, ntasks, nt), dtype=X.dtype, device=X.device)
+    _need(yhat_out, "yhat_out", (nobs, ntasks, nt), X.dtype)
+    if out is None:
+        out = torch.empty((ntasks, nt, nf), dtype=X.dtype, device=X.device)
+    if loss_out is None:
+        loss_out = torch.empty((1,), dtype=X.dtype, device=X.device)
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    capi.call(f"glmb_gradient_loss_{sfx}", _ptr(X), _ptr(M), _ptr(Y), _ptr(out), _ptr(yhat_out), _ptr(loss_out),
+              nf, nt, ntasks, nobs, float(lam), float(alpha), flags, ws_ptr, ws_bytes, _stream(stream))
+    return out, loss_out, yhat_out
+
+
 def gradient_partial(X, M, Y, out=None, yhat_out=None, workspace=None, stream=None):
     """sum_obs (Yhat - Y) X as float64 (no factor 2, no elastic-net term)."""
     sfx = SUFFIX[X.dtype]

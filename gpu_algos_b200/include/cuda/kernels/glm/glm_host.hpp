@@ -131,6 +131,32 @@ Tensor3D<T> gradient(const Tensor3D<T>& X, const Tensor3D<T>& M, const Tensor3D<
     return grad;
 }
 
+// loss = sum (Yhat - Y)^2 + lambda*(alpha*sum|M| + (1-alpha)*sum M^2), one
+// element (glm_loss_myyhat.cuh:365-401 in gpu_algos), sums carried in arith_t.
+template <typename T>
+Tensor3D<T> loss(const Tensor3D<T>& M, const Tensor3D<T>& Y, const Tensor3D<T>& Yhat, double lambda, double alpha) {
+    using A = arith_t<T>;
+    Tensor3D<T> out(1, 1, 1);
+    const long size_Y = Y.cols() * Y.rows() * Y.sheets(), size_M = M.cols() * M.rows() * M.sheets();
+    const T* y = Y.data();
+    const T* yh = Yhat.data();
+    const T* m = M.data();
+    A err = 0, l1 = 0, l2 = 0;
+    for (long i = 0; i < size_Y; ++i) {
+        const A e = up(yh[i]) - up(y[i]);
+        err += e * e;
+    }
+    for (long i = 0; i < size_M; ++i) {
+        const A v = up(m[i]);
+        if constexpr (std::is_floating_point_v<A>) l1 += v < A(0) ? -v : v;
+        else l1 += is_negative(m[i]) ? A(0) - v : v;
+        l2 += v * v;
+    }
+    const A lam = up(from_double<T>(lambda)), alp = up(from_double<T>(alpha));
+    out(0, 0, 0) = down<T>(err + lam * (alp * l1 + (A(1) - alp) * l2));
+    return out;
+}
+
 // ---- typed bridge to the C ABI --------------------------------------------
 #define GLMB_HOST_BRIDGE(T, CT, SFX)                                                                \
     inline int abi_predict(const T* X, const T* M, T* Yhat, long nf, long nt, long ntasks, long nobs, \
@@ -146,6 +172,13 @@ Tensor3D<T> gradient(const Tensor3D<T>& X, const Tensor3D<T>& M, const Tensor3D<
                                    reinterpret_cast<const CT*>(Y), reinterpret_cast<CT*>(grad),     \
                                    reinterpret_cast<CT*>(Yhat), nf, nt, ntasks, nobs, lambda, alpha, \
                                    flags, nullptr, 0, reinterpret_cast<glmb_stream_t>(s));          \
+    }                                                                                               \
+    inline int abi_loss(const T* M, const T* Y, const T* Yhat, T* loss, long nf, long nt, long ntasks,   \
+                        long nobs, double lambda, double alpha, cudaStream_t s) {                   \
+        return glmb_loss_##SFX(reinterpret_cast<const CT*>(M), reinterpret_cast<const CT*>(Y),      \
+                               reinterpret_cast<const CT*>(Yhat), reinterpret_cast<CT*>(loss), nf,  \
+                               nt, ntasks, nobs, lambda, alpha, nullptr, 0,                         \
+                               reinterpret_cast<glmb_stream_t>(s));                                 \
     }                                                                                               \
     inline const char* abi_suffix(const T*) { return #SFX; }
 

@@ -128,6 +128,53 @@ GLMB_DECLARE_GRADIENT(u32, uint32_t)
 GLMB_DECLARE_GRADIENT(u64, uint64_t)
 
 /* ------------------------------------------------------------------------
+ * Loss (the objective):
+ *   loss[0] = sum (Yhat - Y)^2 + lambda*(alpha*sum|M| + (1-alpha)*sum M^2)
+ * over every target, task and observation, lambda and alpha taken in T.
+ * Replaces Glm_loss_myyhat_kernel<T>::run_device_kernel
+ * (include/cuda/kernels/glm/glm_loss_myyhat.cuh:331-363; host definition
+ * :365-401).  Y == NULL means zeros.  float/double/half sum in double,
+ * integer types modulo 2^bits (bit-exact with the reference).  Scratch:
+ * the gradient workspace of the same shape is enough (or NULL: stream-
+ * ordered allocation).  Two launches, one streaming pass over Y and Yhat.
+ * ---------------------------------------------------------------------- */
+#define GLMB_DECLARE_LOSS(SFX, T)                                                       \
+    int glmb_loss_##SFX(const T* M, const T* Y, const T* Yhat, T* loss,                 \
+                        int64_t nfeatures, int64_t ntargets, int64_t ntasks,            \
+                        int64_t nobs, double lambda, double alpha, void* workspace,     \
+                        size_t workspace_bytes, glmb_stream_t stream);
+
+GLMB_DECLARE_LOSS(f16, uint16_t)
+GLMB_DECLARE_LOSS(f32, float)
+GLMB_DECLARE_LOSS(f64, double)
+GLMB_DECLARE_LOSS(i8, int8_t)
+GLMB_DECLARE_LOSS(i16, int16_t)
+GLMB_DECLARE_LOSS(i32, int32_t)
+GLMB_DECLARE_LOSS(i64, int64_t)
+GLMB_DECLARE_LOSS(u8, uint8_t)
+GLMB_DECLARE_LOSS(u16, uint16_t)
+GLMB_DECLARE_LOSS(u32, uint32_t)
+GLMB_DECLARE_LOSS(u64, uint64_t)
+
+/* ------------------------------------------------------------------------
+ * Gradient and loss from one call (float32/float64): glmb_gradient_* with
+ * GLMB_GRAD_WRITE_YHAT (Yhat required), then glmb_loss_* on (M, Y, Yhat)
+ * with the same lambda and alpha (the loss always carries the elastic-net
+ * term; `flags` governs the gradient's).  X is read once; the loss adds one
+ * read of Y and Yhat.  No single reference call does both; it replaces the
+ * reference's xyyhat gradient followed by its loss kernel on the `temp`
+ * prediction.
+ * ---------------------------------------------------------------------- */
+int glmb_gradient_loss_f32(const float* X, const float* M, const float* Y, float* grad_M, float* Yhat,
+                           float* loss, int64_t nfeatures, int64_t ntargets, int64_t ntasks, int64_t nobs,
+                           double lambda, double alpha, uint32_t flags, void* workspace,
+                           size_t workspace_bytes, glmb_stream_t stream);
+int glmb_gradient_loss_f64(const double* X, const double* M, const double* Y, double* grad_M,
+                           double* Yhat, double* loss, int64_t nfeatures, int64_t ntargets, int64_t ntasks,
+                           int64_t nobs, double lambda, double alpha, uint32_t flags, void* workspace,
+                           size_t workspace_bytes, glmb_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Gradient that allocates no device memory (float32).  No counterpart in
  * the reference: it exists for callers that may not allocate -- a host that
  * owns every device buffer and passes a plugin only its inputs and outputs,

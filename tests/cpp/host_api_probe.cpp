@@ -12,6 +12,7 @@
 #include "common/types/tensor3d.hpp"
 #include "cuda/kernels/glm/glm_gradient_naive.cuh"
 #include "cuda/kernels/glm/glm_gradient_xyyhat.cuh"
+#include "cuda/kernels/glm/glm_loss_myyhat.cuh"
 #include "cuda/kernels/glm/glm_predict_naive.cuh"
 #include "cxxopts.hpp"
 
@@ -48,6 +49,15 @@ void host_predict(const T* X, const T* M, T* Yhat, long nf, long nt, long ntasks
     std::memcpy(Yhat, y.data(), y.vector_.size() * sizeof(T));
 }
 
+template <typename T>
+void host_loss(const T* M, const T* Y, const T* Yhat, T* loss, long nf, long nt, long ntasks, long nobs,
+               double lambda, double alpha) {
+    Glm_loss_myyhat_kernel<T> k(Glm_loss_myyhat_spec("float", nf, nt, ntasks, nobs, lambda, alpha, 512));
+    const Tensor3D<T> l = k.run_host_kernel(make(M, nf, nt, ntasks), make(Y, nt, ntasks, nobs),
+                                            make(Yhat, nt, ntasks, nobs));
+    loss[0] = l.data()[0];
+}
+
 std::string g_text;
 
 }  // namespace
@@ -61,6 +71,10 @@ extern "C" {
     }                                                                                                     \
     void probe_predict_##SFX(const T* X, const T* M, T* Yh, long nf, long nt, long ntasks, long nobs) {  \
         host_predict<T>(X, M, Yh, nf, nt, ntasks, nobs);                                                  \
+    }                                                                                                     \
+    void probe_loss_##SFX(const T* M, const T* Y, const T* Yh, T* loss, long nf, long nt, long ntasks,   \
+                          long nobs, double lambda, double alpha) {                                       \
+        host_loss<T>(M, Y, Yh, loss, nf, nt, ntasks, nobs, lambda, alpha);                                \
     }                                                                                                     \
     void probe_randomize_##SFX(T* out, long n, long seed) {                                               \
         Tensor3D<T> t(n, 1, 1);                                                                           \

@@ -29,7 +29,7 @@ def _exported():
 def test_library_loads_and_exports_every_declared_symbol():
     L = capi.lib()
     declared = _declared_functions()
-    assert len(declared) == 4 + 3 * 11 + 8 * 2 + 1 + 6 + 2
+    assert len(declared) == 4 + 4 * 11 + 9 * 2 + 1 + 6 + 2
     exported = _exported()
     missing = [n for n in declared if n not in exported]
     assert not missing, missing

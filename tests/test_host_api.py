@@ -28,6 +28,7 @@ def probe(tmp_path_factory):
         getattr(L, f"probe_gradient_{s}").argtypes = [P, P, P, P, L64, L64, L64, L64, D, D, I, I]
         getattr(L, f"probe_predict_{s}").argtypes = [P, P, P, L64, L64, L64, L64]
         getattr(L, f"probe_randomize_{s}").argtypes = [P, L64, L64]
+        getattr(L, f"probe_loss_{s}").argtypes = [P, P, P, P, L64, L64, L64, L64, D, D]
     L.probe_parse.argtypes = [I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p)]
     L.probe_parse.restype = I
     return L
@@ -97,6 +98,28 @@ def test_host_kernels_match_oracle(probe, oracle, golden):
                               oracle.gradient(Xi, Mi, Yi, 2.9, 0.5, True))
 
 
+def test_host_loss_matches_oracle(probe, oracle):
+    rng = np.random.default_rng(5)
+    for dt in (np.float32, np.float64, np.int32, np.uint8, np.int64):
+        dt = np.dtype(dt)
+        for (nobs, ntasks, nf, nt) in [(1, 1, 1, 1), (300, 3, 7, 5), (0, 2, 4, 3)]:
+            if dt.kind in "iu":
+                lo = 0 if dt.kind == "u" else -50
+                mk = lambda s: rng.integers(lo, 50, s).astype(dt)  # noqa: E731
+            else:
+                mk = lambda s: rng.uniform(-1, 1, s).astype(dt)  # noqa: E731
+            M, Y, Yh = mk((ntasks, nt, nf)), mk((nobs, ntasks, nt)), mk((nobs, ntasks, nt))
+            for lam, alpha in [(0.0, 0.0), (2.0, 0.5), (3.0, 1.0)]:
+                got = np.zeros((1,), dtype=dt)
+                getattr(probe, f"probe_loss_{SFX[dt]}")(_p(M), _p(Y), _p(Yh), _p(got), nf, nt, ntasks, nobs,
+                                                      lam, alpha)
+                ref = oracle.loss(M, Y, Yh, lam, alpha)
+                if dt.kind in "iu":
+                    assert got[0] == ref[0], (dt, lam, alpha)
+                else:
+                    assert abs(float(got[0]) - float(ref[0])) <= 1e-5 * abs(float(ref[0])) + 1e-30
+
+
 def test_seeded_initialisation_is_mt19937_64_uniform(probe):
     a = np.zeros(1000, np.float32)
     probe.probe_randomize_f32(_p(a), 1000, 42)
@@ -130,7 +153,7 @@ def test_option_parser(probe):
         assert rc == 1, (bad, out)
 
 
-@pytest.mark.parametrize("exe", ["glm_predict_naive", "glm_gradient_naive", "glm_gradient_xyyhat"])
+@pytest.mark.parametrize("exe", ["glm_predict_naive", "glm_gradient_naive", "glm_gradient_xyyhat", "glm_loss_myyhat"])
 def test_executables_help_and_bad_options(exe):
     path = os.path.join(BIN, exe)
     assert os.path.exists(path), "build with make -C gpu_algos_b200"
