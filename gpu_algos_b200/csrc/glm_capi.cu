@@ -80,6 +80,9 @@ int check_device() {
 
 template <typename T>
 constexpr bool kRowsType = std::is_same_v<T, float> || std::is_same_v<T, double>;
+// element types the fused rows kernel is built for (half: float arithmetic, 16-byte loads of 8 values)
+template <typename T>
+constexpr bool kRowsKernelType = kRowsType<T> || std::is_same_v<T, __half>;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -97,7 +100,7 @@ int predict_impl(const T* X, const T* M, T* Yhat, int64_t nf, int64_t nt, int64_
         return int(cudaMemsetAsync(Yhat, 0, size_t(nout) * sizeof(T), stream));
     }
     if (X == nullptr || M == nullptr) return GLMB_ERR_INVALID_VALUE;
-    if constexpr (kRowsType<T>) {
+    if constexpr (kRowsKernelType<T>) {
         const RowsPlan p = rows_plan<T>(nf, nt, ntasks, nobs, aligned16(X), false);
         if (p.ok) {
             RowsArgs a{X, M, nullptr, Yhat, nullptr, nf, nt, ntasks, nobs, p.obs_per_cta,
@@ -116,7 +119,7 @@ size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
     if (check_device() != GLMB_OK) return 0;
     size_t need = 0;
     bool all_rows = false;
-    if constexpr (kRowsType<T>) {
+    if constexpr (kRowsKernelType<T>) {
         const RowsPlan a = rows_plan<T>(nf, nt, ntasks, nobs, true, true);
         const RowsPlan b = rows_plan<T>(nf, nt, ntasks, nobs, false, true);
         all_rows = a.ok && b.ok;
@@ -188,7 +191,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
     if (nobs > 0 && (X == nullptr || (!y_zero && Y == nullptr))) return GLMB_ERR_INVALID_VALUE;
     const T* Yin = y_zero ? nullptr : Y;
     T* Yhat_out = write_yhat ? Yhat : nullptr;
-    if constexpr (kRowsType<T>) {
+    if constexpr (kRowsKernelType<T>) {
         const RowsPlan p = rows_plan<T>(nf, nt, ntasks, nobs, aligned16(X), true);
         if (p.ok) {
             Scratch sc(ws, ws_bytes, round_up(p.part_doubles * sizeof(double), 256), stream);

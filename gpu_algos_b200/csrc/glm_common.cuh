@@ -170,6 +170,49 @@ struct VecLoad<double, 2> {
     }
 };
 template <>
+struct VecLoad<__half, 8> {
+    __device__ __forceinline__ static void load(const __half* p, __half (&v)[8]) {
+        uint32_t r[4];
+        asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                     : "l"(p));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // element 2i is the low half of word i
+            v[2 * i] = __ushort_as_half(static_cast<unsigned short>(r[i] & 0xffffu));
+            v[2 * i + 1] = __ushort_as_half(static_cast<unsigned short>(r[i] >> 16));
+        }
+    }
+};
+template <>
+struct VecLoad<__half, 4> {
+    __device__ __forceinline__ static void load(const __half* p, __half (&v)[4]) {
+        uint32_t r[2];
+        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "l"(p));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            v[2 * i] = __ushort_as_half(static_cast<unsigned short>(r[i] & 0xffffu));
+            v[2 * i + 1] = __ushort_as_half(static_cast<unsigned short>(r[i] >> 16));
+        }
+    }
+};
+template <>
+struct VecLoad<__half, 2> {
+    __device__ __forceinline__ static void load(const __half* p, __half (&v)[2]) {
+        uint32_t r;
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+        v[0] = __ushort_as_half(static_cast<unsigned short>(r & 0xffffu));
+        v[1] = __ushort_as_half(static_cast<unsigned short>(r >> 16));
+    }
+};
+template <>
+struct VecLoad<__half, 1> {
+    __device__ __forceinline__ static void load(const __half* p, __half (&v)[1]) {
+        unsigned short r;
+        asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
+        v[0] = __ushort_as_half(r);
+    }
+};
+template <>
 struct VecLoad<float, 1> {
     __device__ __forceinline__ static void load(const float* p, float (&v)[1]) {
         asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v[0]) : "l"(p));

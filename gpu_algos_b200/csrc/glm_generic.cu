@@ -215,6 +215,8 @@ GLMB_INSTANTIATE_GENERIC(uint16_t)
 GLMB_INSTANTIATE_GENERIC(uint32_t)
 GLMB_INSTANTIATE_GENERIC(uint64_t)
 
+template int finalize_launch<__half, double>(const double*, int64_t, int64_t, const __half*, __half*,
+                                             double*, double, double, bool, cudaStream_t);
 template int finalize_launch<float, double>(const double*, int64_t, int64_t, const float*, float*,
                                             double*, double, double, bool, cudaStream_t);
 template int finalize_launch<double, double>(const double*, int64_t, int64_t, const double*,

@@ -1,4 +1,6 @@
-// glm_rows.cuh -- fused row-streaming GLM kernel for float / double.
+// glm_rows.cuh -- fused row-streaming GLM kernel for float / double / half
+// (half: float arithmetic on 16-byte loads of 8 values, half the HBM bytes
+// of float per feature).
 //
 // One pass over X computes, for every row x = X[obs, task, :],
 //     yhat_t = sum_f M[task, t, f] * x_f          (t < ntargets)
@@ -56,12 +58,61 @@ template <typename T, int VEC, int CPL, int NT>
 struct RowsShape {
     static constexpr int FPL = CPL * VEC;  // features per lane
     static constexpr int WORDS = FPL * int(sizeof(T)) / 4 + NT;
-    static constexpr int U_RAW = 20 / WORDS;
+    // register words a batch may take; half rows carry half the bytes per
+    // register, so twice as many of them keep as many bytes in flight
+    static constexpr int U_RAW = (sizeof(T) == 2 ? 40 : 20) / WORDS;
     // rows (or row steps) per batch: a power of two in [1, 8]
     static constexpr int U = U_RAW >= 8 ? 8 : (U_RAW >= 4 ? 4 : (U_RAW >= 2 ? 2 : 1));
     static constexpr int LOG2U = U == 8 ? 3 : (U == 4 ? 2 : (U == 2 ? 1 : 0));
     static constexpr int SLOTS = NT * CPL * kWarp * VEC;  // doubles per warp in smem
     static constexpr size_t SMEM = size_t(kRowsWarps) * SLOTS * sizeof(double);
+};
+
+// Register image of one lane's VEC consecutive elements of a row: the
+// elements themselves, or -- for half with VEC >= 2 -- pairs packed in 32-bit
+// words (element 2i in the low half of word i), converted at use, so a batch
+// of half rows takes half the registers of a batch of float rows.
+template <typename T, int VEC>
+struct XRegs {
+    static constexpr int N = VEC;
+    using W = T;
+    __device__ __forceinline__ static void load(const T* p, W (&w)[N]) { VecLoad<T, VEC>::load(p, w); }
+    template <typename D>
+    __device__ __forceinline__ static D get(const W (&w)[N], int v) {
+        return D(w[v]);
+    }
+};
+template <int VEC>
+struct XRegs<__half, VEC> {
+    static_assert(VEC == 2 || VEC == 4 || VEC == 8, "packed half vectors");
+    static constexpr int N = VEC / 2;
+    using W = uint32_t;
+    __device__ __forceinline__ static void load(const __half* p, W (&w)[N]) {
+        if constexpr (N == 4) {
+            asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                         : "l"(p));
+        } else if constexpr (N == 2) {
+            asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "l"(p));
+        } else {
+            asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(w[0]) : "l"(p));
+        }
+    }
+    template <typename D>
+    __device__ __forceinline__ static D get(const W (&w)[N], int v) {
+        const uint32_t x = w[v >> 1];
+        return D(__half2float(__ushort_as_half(static_cast<unsigned short>((v & 1) ? (x >> 16) : (x & 0xffffu)))));
+    }
+};
+template <>
+struct XRegs<__half, 1> {
+    static constexpr int N = 1;
+    using W = __half;
+    __device__ __forceinline__ static void load(const __half* p, W (&w)[1]) { VecLoad<__half, 1>::load(p, w); }
+    template <typename D>
+    __device__ __forceinline__ static D get(const W (&w)[1], int) {
+        return D(__half2float(w[0]));
+    }
 };
 
 // FULL: one row per warp (S = 32).  The U rows of a batch are then reduced
@@ -79,6 +130,9 @@ template <typename T, int VEC, int CPL, int NT, int MODE, bool FULL>
 __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a) {
     using D = typename Arith<T>::Dot;
     using Shape = RowsShape<T, VEC, CPL, NT>;
+    using XR = XRegs<T, VEC>;
+    using XW = typename XR::W;
+    constexpr int XN = XR::N;
     constexpr int U = Shape::U;
     constexpr int LOG2U = Shape::LOG2U;
     constexpr bool GRAD = MODE != kRowsPredict;
@@ -151,7 +205,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 
     // Issue the loads of one batch: U steps of R rows starting at `base`.
     // FULL batches load y only for the row whose residual this lane forms.
-    auto load = [&](T (&xb)[U][CPL][VEC], D (&yb)[U][NT], int64_t base) {
+    auto load = [&](XW (&xb)[U][CPL][XN], D (&yb)[U][NT], int64_t base) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t obs = base + int64_t(u) * R + grp;
@@ -161,10 +215,10 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
             for (int c = 0; c < CPL; ++c) {
                 const int64_t f0 = int64_t(c * S + ls) * VEC;
                 if (ok && f0 < nf) {
-                    VecLoad<T, VEC>::load(xrow + f0, xb[u][c]);
+                    XR::load(xrow + f0, xb[u][c]);
                 } else {
 #pragma unroll
-                    for (int v = 0; v < VEC; ++v) xb[u][c][v] = T(0);
+                    for (int v = 0; v < XN; ++v) xb[u][c][v] = XW(0);
                 }
             }
         }
@@ -188,7 +242,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
         }
     };
 
-    auto compute = [&](const T (&xb)[U][CPL][VEC], const D (&yb)[U][NT], int64_t base) {
+    auto compute = [&](const XW (&xb)[U][CPL][XN], const D (&yb)[U][NT], int64_t base) {
         if constexpr (FULL) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
@@ -199,7 +253,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                     for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], D(xb[u][c][v]), d);
+                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], XR::template get<D>(xb[u][c], v), d);
                     vals[u] = d;
                 }
                 // transposed butterfly over the first log2(U) lane bits
@@ -231,7 +285,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                         for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, D(xb[u][c][v]), acc[t][c][v]);
+                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get<D>(xb[u][c], v), acc[t][c][v]);
                     }
                 }
             }
@@ -245,7 +299,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                     for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], D(xb[u][c][v]), d);
+                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], XR::template get<D>(xb[u][c], v), d);
                     for (int off = S >> 1; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
                     if constexpr (MODE != kRowsGrad) {
                         if (ls == 0 && t < nt && obs < obs_end) Yhat[(obs * ntasks + task) * nt + t] = T(d);
@@ -255,7 +309,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                         for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, D(xb[u][c][v]), acc[t][c][v]);
+                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get<D>(xb[u][c], v), acc[t][c][v]);
                     }
                 }
             }
@@ -272,7 +326,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
             }
         }
     };
-    T xa[U][CPL][VEC], xb[U][CPL][VEC];
+    XW xa[U][CPL][XN], xb[U][CPL][XN];
     D ya[U][NT], yb[U][NT];
     int64_t base = obs_begin + int64_t(warp) * U * R;
     if (base < obs_end) load(xa, ya, base);

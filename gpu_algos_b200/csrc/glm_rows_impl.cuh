@@ -1,6 +1,6 @@
 // glm_rows_impl.cuh -- launch planning and dispatch of the rows kernel.
-// Included by glm_rows_f32.cu / glm_rows_f64.cu, one instantiation per file
-// so the two element types compile in parallel.
+// Included by glm_rows_f16.cu / glm_rows_f32.cu / glm_rows_f64.cu, one
+// instantiation per file so the element types compile in parallel.
 #pragma once
 
 #include <algorithm>
@@ -11,8 +11,9 @@ namespace glmb {
 
 template <typename T>
 constexpr int rows_budget() {
-    // register-resident accumulator words per lane (NT * CPL * VEC)
-    return sizeof(T) == 4 ? 32 : 16;
+    // register-resident accumulator words per lane (NT * CPL * VEC): 32 for
+    // float arithmetic (float and half inputs), 16 for double
+    return sizeof(typename Arith<T>::Dot) == 4 ? 32 : 16;
 }
 
 template <typename T, int VEC, int CPL, int NT>
@@ -52,6 +53,10 @@ int rows_dispatch(int vec, int cpl, int ntmax, F&& f) {
     };
     if (vec == VW) return by_cpl.template operator()<VW>();
     if (vec == 1) return by_cpl.template operator()<1>();
+    if constexpr (VW == 8) {  // half: narrower vectors too (see rows_plan)
+        if (vec == 4) return by_cpl.template operator()<4>();
+        if (vec == 2) return by_cpl.template operator()<2>();
+    }
     return GLMB_ERR_UNSUPPORTED;
 }
 
@@ -88,6 +93,16 @@ RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool ve
     if (nf <= 0 || nt <= 0 || ntasks <= 0 || nobs < 0) return p;
     constexpr int VW = 16 / int(sizeof(T));
     p.vec = (vec_aligned && nf % VW == 0) ? VW : 1;
+    if constexpr (VW == 8) {
+        // half: the widest vector that still spreads a row over a full warp
+        // (the full-warp kernel reduces a batch of rows with the transposed
+        // butterfly; a 16-lane row would take the per-segment reduction)
+        if (vec_aligned) {
+            int v = VW;
+            while (v > 1 && (nf % v != 0 || nf / v < kWarp)) v >>= 1;
+            p.vec = v;
+        }
+    }
     const int64_t nvec = nf / p.vec;
     int cpl = 0;
     for (int c : {1, 2, 4, 8})

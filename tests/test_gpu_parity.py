@@ -316,3 +316,29 @@ def test_dense_path_at_the_solution(oracle):
     ref = oracle.gradient_acc64(X, M, Y, 0.001, 0.0, True)
     assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 1e-4
     assert np.abs(g - ref).max() <= 2e-4 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("shape", [(100000, 1, 128, 1), (20000, 2, 64, 4), (5001, 3, 1024, 1), (777, 2, 40, 3)])
+def test_half_rows_path(shape, oracle):
+    """float16 inputs on the fused rows kernel (8 values per 16-byte load,
+    float arithmetic): within the driver's half tolerance of the oracle."""
+    nobs, ntasks, nf, nt = shape
+    rng = np.random.default_rng(nobs + nf)
+    X = (rng.uniform(-1, 1, (nobs, ntasks, nf)) / 4).astype(np.float16)
+    M = rng.normal(size=(ntasks, nt, nf)).astype(np.float16)
+    Y = (np.einsum("otf,tkf->otk", X.astype(np.float64), M.astype(np.float64))
+         + 0.05 * rng.normal(size=(nobs, ntasks, nt))).astype(np.float16)
+    g, yh = G.gradient(X, M, Y, 0.1, 0.5, reg=True, want_yhat=True)
+    assert capi.last_path() == "rows"
+    og = oracle.gradient(X, M, Y, 0.1, 0.5, True)
+    exact = (2 * np.einsum("otk,otf->tkf", np.einsum("otf,tkf->otk", X.astype(np.float64), M.astype(np.float64))
+                           - Y.astype(np.float64), X.astype(np.float64))
+             + 0.1 * (0.5 * np.sign(M.astype(np.float64)) + 2 * 0.5 * M.astype(np.float64)))
+    scale = np.abs(exact).max()
+    # float arithmetic (residuals ~0.05 out of predictions ~5 lose a few bits
+    # to cancellation), one rounding to half at the end: within 2^-8, tighter
+    # than the driver's half tolerance 2^-7
+    assert np.all(np.abs(g.astype(np.float64) - exact) <= 2.0 ** -8 * (np.abs(exact) + 1e-2 * scale))
+    _check_float(g, og, np.float16, scale=scale * 1e-2, what="half grad vs oracle")
+    oy = oracle.predict(X, M)  # mixed signs: predictions near zero are judged on the data's scale
+    _check_float(yh, oy, np.float16, scale=np.abs(oy.astype(np.float64)).max() * 1e-2, what="half yhat")
