@@ -25,6 +25,7 @@ PEER_HANDLE_BYTES = 64
 GRAD_REGULARIZE = 0x1
 GRAD_WRITE_YHAT = 0x2
 GRAD_Y_ZERO = 0x4
+GRAD_LOGISTIC = 0x8
 
 #: the eleven element types of the reference mains, by C-ABI suffix
 SUFFIXES = ("f16", "f32", "f64", "i8", "i16", "i32", "i64", "u8", "u16", "u32", "u64")

@@ -171,8 +171,10 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
                   uint32_t flags, void* ws, size_t ws_bytes, cudaStream_t stream,
                   glmb_peer_group* peer = nullptr) {
     if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0) return GLMB_ERR_INVALID_VALUE;
-    if (flags & ~(GLMB_GRAD_REGULARIZE | GLMB_GRAD_WRITE_YHAT | GLMB_GRAD_Y_ZERO))
+    if (flags & ~(GLMB_GRAD_REGULARIZE | GLMB_GRAD_WRITE_YHAT | GLMB_GRAD_Y_ZERO | GLMB_GRAD_LOGISTIC))
         return GLMB_ERR_INVALID_VALUE;
+    const bool logistic = (flags & GLMB_GRAD_LOGISTIC) != 0;
+    if (logistic && !std::is_floating_point_v<T> && !std::is_same_v<T, __half>) return GLMB_ERR_INVALID_VALUE;
     const bool reg = (flags & GLMB_GRAD_REGULARIZE) != 0;
     const bool write_yhat = (flags & GLMB_GRAD_WRITE_YHAT) != 0;
     const bool y_zero = (flags & GLMB_GRAD_Y_ZERO) != 0;
@@ -181,7 +183,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
     if (write_yhat && nout > 0 && Yhat == nullptr) return GLMB_ERR_INVALID_VALUE;
     int st = check_device();
     if (st != GLMB_OK) return st;
-    if (nf == 0) {
+    if (nf == 0 && !logistic) {
         set_last_path("memset");
         if (write_yhat && nout > 0)
             return int(cudaMemsetAsync(Yhat, 0, size_t(nout) * sizeof(T), stream));
@@ -199,7 +201,9 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
             RowsArgs a{X, M, Yin, Yhat_out, sc.as<double>(), nf, nt, ntasks, nobs, p.obs_per_cta,
                        p.ctas_per_task, 0, p.ctas_per_task, p.seg_log2};
             set_last_path("rows");
-            st = rows_launch<T>(p, write_yhat ? kRowsGradYhat : kRowsGrad, a, stream);
+            const int mode = logistic ? (write_yhat ? kRowsGradLogitYhat : kRowsGradLogit)
+                                      : (write_yhat ? kRowsGradYhat : kRowsGrad);
+            st = rows_launch<T>(p, mode, a, stream);
             if (st != GLMB_OK) return st;
             if constexpr (kRowsType<T>) {
                 if (peer != nullptr)
@@ -211,7 +215,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
         }
     }
     if constexpr (std::is_same_v<T, float>) {
-        if (nobs > 0 && dense_f32_supported(nf, nt, ntasks, nobs, X, M)) {
+        if (!logistic && nobs > 0 && dense_f32_supported(nf, nt, ntasks, nobs, X, M)) {
             const DensePlan dp = dense_f32_plan(nf, nt, ntasks, nobs);
             const int64_t total = ntasks * nt * nf;
             const size_t local_bytes = peer != nullptr ? round_up(size_t(total) * sizeof(double), 256) : 0;
@@ -230,7 +234,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
         }
     }
     if constexpr (std::is_same_v<T, double>) {
-        if (tiles_f64_supported(nf, nt, ntasks, X)) {
+        if (!logistic && tiles_f64_supported(nf, nt, ntasks, X)) {
             const TilesPlan tp = tiles_f64_plan(nf, nt, ntasks, nobs);
             const size_t part_bytes = round_up(tp.part_doubles * sizeof(double), 256);
             Scratch sc(ws, ws_bytes, part_bytes + 256, stream);
@@ -256,11 +260,11 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
         if (peer != nullptr) {
             PeerFinish<T> fin{peer, M, grad, partial_out, lambda, alpha, reg, nullptr, ntasks * nt * nf, stream};
             return generic_gradient<T>(X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
-                                       alpha, reg, ws, ws_bytes, stream, &PeerFinish<T>::call, &fin);
+                                       alpha, reg, ws, ws_bytes, stream, &PeerFinish<T>::call, &fin, logistic);
         }
     }
     return generic_gradient<T>(X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
-                               alpha, reg, ws, ws_bytes, stream);
+                               alpha, reg, ws, ws_bytes, stream, nullptr, nullptr, logistic);
 }
 
 template <typename T>
@@ -415,6 +419,7 @@ GLMB_DEFINE_BASIC(u64, uint64_t, uint64_t)
                                  double lambda, double alpha, uint32_t flags, void* workspace,     \
                                  size_t workspace_bytes, glmb_stream_t stream) {                   \
         if (loss == nullptr || (Yhat == nullptr && nobs * nt * ntasks > 0)) return GLMB_ERR_INVALID_VALUE; \
+        if (flags & GLMB_GRAD_LOGISTIC) return GLMB_ERR_UNSUPPORTED; /* the loss is the squared error */ \
         return guarded([&] {                                                                       \
             const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);                         \
             int st = glmb::gradient_impl<T>(X, M, Y, grad_M, Yhat, nullptr, nf, nt, ntasks, nobs,  \

@@ -149,6 +149,14 @@ __device__ __forceinline__ T finalize_value(S sum, T m, double lambda, double al
     return from_arith<T>(g);
 }
 
+// Logistic function 1 / (1 + e^-z) for the logistic link (expf / exp; an
+// infinite e^-z gives 0, never NaN).
+template <typename D>
+__device__ __forceinline__ D sigmoid(D z) {
+    if constexpr (std::is_same_v<D, double>) return 1.0 / (1.0 + exp(-z));
+    else return 1.0f / (1.0f + expf(-z));
+}
+
 // ---- global loads that bypass L1 (X is streamed exactly once) -------------
 template <typename T, int VEC>
 struct VecLoad;

@@ -13,11 +13,13 @@ constexpr int kGenTY = 8;   // observation lanes per block
 constexpr int kGenTT = 8;   // targets per register tile
 
 // One thread per (obs, task, target): yhat = <X row, M row>, E = yhat - y.
+// logistic (float/double): yhat = sigmoid(<X row, M row>), E = (yhat - y) / 2
+// (the finalize's factor 2 then gives the logistic log-likelihood gradient).
 template <typename T>
 __global__ void __launch_bounds__(256)
     glm_residual_kernel(const T* __restrict__ X, const T* __restrict__ M, const T* __restrict__ Y,
                         T* __restrict__ Yhat, typename Arith<T>::Dot* __restrict__ E, int64_t nf,
-                        int64_t nt, int64_t ntasks, int64_t nobs) {
+                        int64_t nt, int64_t ntasks, int64_t nobs, int logistic) {
     using D = typename Arith<T>::Dot;
     const int64_t n = nobs * ntasks * nt;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
@@ -29,8 +31,15 @@ __global__ void __launch_bounds__(256)
         const T* m = M + (task * nt + t) * nf;
         D d = D(0);
         for (int64_t f = 0; f < nf; ++f) d += to_arith<D>(m[f]) * to_arith<D>(x[f]);
+        if constexpr (std::is_floating_point_v<D>) {
+            if (logistic) d = sigmoid(d);
+        }
         if (Yhat != nullptr) Yhat[i] = from_arith<T>(d);
-        if (E != nullptr) E[i] = d - (Y != nullptr ? to_arith<D>(Y[i]) : D(0));
+        if (E != nullptr) {
+            const D e = d - (Y != nullptr ? to_arith<D>(Y[i]) : D(0));
+            if constexpr (std::is_floating_point_v<D>) E[i] = logistic ? D(0.5) * e : e;
+            else E[i] = e;
+        }
     }
 }
 
@@ -144,7 +153,7 @@ int generic_predict(const T* X, const T* M, T* Yhat, int64_t nf, int64_t nt, int
     const int64_t n = nobs * ntasks * nt;
     if (n == 0) return GLMB_OK;
     glm_residual_kernel<T><<<grid_for(n, 256), 256, 0, stream>>>(X, M, nullptr, Yhat, nullptr, nf,
-                                                                  nt, ntasks, nobs);
+                                                                  nt, ntasks, nobs, 0);
     count_launch();
     return launch_status();
 }
@@ -167,7 +176,7 @@ template <typename T>
 int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
                      int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda,
                      double alpha, bool reg, void* ws, size_t ws_bytes, cudaStream_t stream,
-                     PartsFinisher fin, void* fin_ctx) {
+                     PartsFinisher fin, void* fin_ctx, bool logistic) {
     using D = typename Arith<T>::Dot;
     using A = typename Arith<T>::Acc;
     const GenericPlan p = generic_plan<T>(nf, nt, ntasks, nobs);
@@ -179,7 +188,7 @@ int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, doubl
     const int64_t n = nobs * ntasks * nt;
     if (n > 0) {
         glm_residual_kernel<T><<<grid_for(n, 256), 256, 0, stream>>>(X, M, Y, Yhat, E, nf, nt,
-                                                                      ntasks, nobs);
+                                                                      ntasks, nobs, logistic ? 1 : 0);
         count_launch();
         if ((st = launch_status()) != GLMB_OK) return st;
     }
@@ -201,7 +210,7 @@ int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, doubl
                                     cudaStream_t);                                                 \
     template int generic_gradient<T>(const T*, const T*, const T*, T*, T*, double*, int64_t,       \
                                      int64_t, int64_t, int64_t, double, double, bool, void*,       \
-                                     size_t, cudaStream_t, PartsFinisher, void*);
+                                     size_t, cudaStream_t, PartsFinisher, void*, bool);
 
 GLMB_INSTANTIATE_GENERIC(__half)
 GLMB_INSTANTIATE_GENERIC(float)

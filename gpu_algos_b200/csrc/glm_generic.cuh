@@ -21,12 +21,14 @@ int generic_predict(const T* X, const T* M, T* Yhat, int64_t nf, int64_t nt, int
 // reduction writes sum (Yhat - Y) X as double instead of the gradient.
 // With `fin` set, fin(fin_ctx, part, nparts) replaces that reduction: part is
 // laid out [e][nparts] in the Acc type (double for float/double inputs).
+// `logistic` (floating types): residuals sigmoid(x.m) - y, predictions
+// sigmoid(x.m), the gradient of the logistic negative log-likelihood.
 using PartsFinisher = int (*)(void* ctx, const void* part, int64_t nparts);
 template <typename T>
 int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
                      int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda,
                      double alpha, bool reg, void* ws, size_t ws_bytes, cudaStream_t stream,
-                     PartsFinisher fin = nullptr, void* fin_ctx = nullptr);
+                     PartsFinisher fin = nullptr, void* fin_ctx = nullptr, bool logistic = false);
 
 // Reduction of per-part sums part[e * nparts + c] over c in a fixed order, one
 // warp per output element e < total, then either

@@ -31,7 +31,18 @@
 
 namespace glmb {
 
-enum RowsMode : int { kRowsGrad = 0, kRowsGradYhat = 1, kRowsPredict = 2 };
+// kRowsGradLogit*: logistic link -- the residual is sigmoid(x.m) - y, scaled
+// by 1/2 so that the finalize's 2*sum gives the gradient of the logistic
+// negative log-likelihood; the written prediction is sigmoid(x.m).
+enum RowsMode : int {
+    kRowsGrad = 0,
+    kRowsGradYhat = 1,
+    kRowsPredict = 2,
+    kRowsGradLogit = 3,
+    kRowsGradLogitYhat = 4,
+    kRowsModes = 5
+};
+
 
 constexpr int kRowsWarps = 8;
 constexpr int kRowsThreads = kRowsWarps * kWarp;
@@ -136,6 +147,8 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
     constexpr int U = Shape::U;
     constexpr int LOG2U = Shape::LOG2U;
     constexpr bool GRAD = MODE != kRowsPredict;
+    constexpr bool LOGIT = MODE == kRowsGradLogit || MODE == kRowsGradLogitYhat;
+    constexpr bool WRITE = MODE == kRowsGradYhat || MODE == kRowsPredict || MODE == kRowsGradLogitYhat;
     extern __shared__ double smem_acc[];
 
     const T* __restrict__ X = static_cast<const T*>(a.X);
@@ -271,14 +284,15 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                 }
 #pragma unroll
                 for (int o = 16 >> LOG2U; o > 0; o >>= 1) vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], o);
-                const D d = vals[0];  // dot product of row u_mine
-                if constexpr (MODE != kRowsGrad) {
+                D d = vals[0];  // dot product of row u_mine
+                if constexpr (LOGIT) d = sigmoid(d);
+                if constexpr (WRITE) {
                     const int64_t obs = base + u_mine;
                     if ((lane & ((32 >> LOG2U) - 1)) == 0 && t < nt && obs < obs_end)
                         Yhat[(obs * ntasks + task) * nt + t] = T(d);
                 }
                 if constexpr (GRAD) {
-                    const D r_mine = d - yb[0][t];
+                    const D r_mine = LOGIT ? D(0.5) * (d - yb[0][t]) : d - yb[0][t];
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
                         const D r = __shfl_sync(0xffffffffu, r_mine, u << (5 - LOG2U));
@@ -301,11 +315,12 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                         for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], XR::template get<D>(xb[u][c], v), d);
                     for (int off = S >> 1; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-                    if constexpr (MODE != kRowsGrad) {
+                    if constexpr (LOGIT) d = sigmoid(d);
+                    if constexpr (WRITE) {
                         if (ls == 0 && t < nt && obs < obs_end) Yhat[(obs * ntasks + task) * nt + t] = T(d);
                     }
                     if constexpr (GRAD) {
-                        const D r = d - yb[u][t];
+                        const D r = LOGIT ? D(0.5) * (d - yb[u][t]) : d - yb[u][t];
 #pragma unroll
                         for (int c = 0; c < CPL; ++c)
 #pragma unroll

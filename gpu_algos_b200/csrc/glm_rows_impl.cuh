@@ -64,13 +64,15 @@ template <typename T, int VEC, int CPL, int NT, bool FULL>
 auto rows_kernel_for(int mode) {
     if (mode == kRowsGrad) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGrad, FULL>;
     if (mode == kRowsGradYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradYhat, FULL>;
+    if (mode == kRowsGradLogit) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradLogit, FULL>;
+    if (mode == kRowsGradLogitYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradLogitYhat, FULL>;
     return &glm_rows_kernel<T, VEC, CPL, NT, kRowsPredict, FULL>;
 }
 
 template <typename T, int VEC, int CPL, int NT, bool FULL>
 int rows_ctas_per_sm(int mode) {
     // cached per instance and mode; every device this library runs on is a B200
-    static int cached[3] = {0, 0, 0};
+    static int cached[kRowsModes] = {0, 0, 0, 0, 0};
     int& c = cached[mode];
     if (c == 0) {
         using Shape = RowsShape<T, VEC, CPL, NT>;

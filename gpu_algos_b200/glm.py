@@ -78,18 +78,21 @@ def workspace_bytes(dtype, nf: int, nt: int, ntasks: int, nobs: int) -> int:
 
 
 def gradient(X, M, Y, lam: float = 0.0, alpha: float = 0.0, regularize: bool = True,
-             yhat_out=None, out=None, workspace=None, stream=None):
+             yhat_out=None, out=None, workspace=None, stream=None, logistic: bool = False):
     """Fused prediction + gradient (+ elastic-net term when ``regularize``).
 
     ``Y=None`` means an all-zero Y.  ``yhat_out`` (optional) receives the
     predictions.  ``workspace`` is an optional CUDA uint8 tensor of at least
-    :func:`workspace_bytes` bytes.
+    :func:`workspace_bytes` bytes.  ``logistic``: logistic link (mu =
+    sigmoid(X M), gradient sum (mu - Y) X of the log-likelihood; predictions mu).
     """
     sfx = SUFFIX[X.dtype]
     nf, nt, ntasks, nobs = _dims(X, M)
     _need(X, "X", (nobs, ntasks, nf), X.dtype)
     _need(M, "M", (ntasks, nt, nf), X.dtype)
     flags = capi.GRAD_REGULARIZE if regularize else 0
+    if logistic:
+        flags |= capi.GRAD_LOGISTIC
     if Y is None:
         flags |= capi.GRAD_Y_ZERO
     else:

@@ -56,6 +56,14 @@ typedef struct CUstream_st* glmb_stream_t;
 #define GLMB_GRAD_REGULARIZE 0x1u /* add lambda*(alpha*sign(M) + 2*(1-alpha)*M)   */
 #define GLMB_GRAD_WRITE_YHAT 0x2u /* also write Yhat = X.M (predictions)           */
 #define GLMB_GRAD_Y_ZERO 0x4u     /* Y is all zeros (Y may be NULL)               */
+/* Logistic link (half/float/double): with mu = 1/(1 + exp(-X.M)) the
+ * gradient is sum_obs (mu - Y) X [+ the elastic-net term], the gradient of
+ * the logistic negative log-likelihood, and Yhat (GLMB_GRAD_WRITE_YHAT)
+ * receives mu.  The reference's predict kernels carry an unused transform
+ * hook for such links (glm_predict_naive.cuh:82-83,550); it applies no link
+ * itself.  Not accepted by glmb_gradient_loss_* (whose loss is the squared
+ * error) or glmb_gradient_noalloc_f32. */
+#define GLMB_GRAD_LOGISTIC 0x8u
 
 /* Library version as an integer (major*10000 + minor*100 + patch). */
 int glmb_version(void);

@@ -58,6 +58,9 @@ def test_argument_validation_happens_before_any_device_call():
     # negative sizes and bad flags are rejected without touching CUDA
     assert L.glmb_gradient_f32(None, None, None, None, None, -1, 1, 1, 1, 0.0, 0.0, 0, None, 0, None) == 1001
     assert L.glmb_gradient_f64(None, None, None, None, None, 4, 1, 1, 8, 0.0, 0.0, 0x100, None, 0, None) == 1001
+    # the logistic link is for floating types only
+    assert L.glmb_gradient_i32(None, None, None, None, None, 4, 1, 1, 8, 0.0, 0.0, capi.GRAD_LOGISTIC, None, 0,
+                               None) == 1001
     assert L.glmb_predict_i32(None, None, None, 3, -2, 1, 1, None) == 1001
     assert L.glmb_prox_step_f32(None, None, -5, 1.0, 0.0, None) == 1001
     assert L.glmb_prox_update_f64(None, None, None, 4, 1, 1, -1.0, 0.0, None) == 1001
