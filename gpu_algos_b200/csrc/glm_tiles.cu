@@ -173,8 +173,24 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
         for (int k = 0; k < kMaxF / 4; ++k) mreg[k] = mb[4 * k];
     }
 
+    // This lane's two y values of a tile (step 2's residual), loaded one tile
+    // ahead: Y streams from DRAM, and a whole tile of work hides its latency
+    // where the contraction of one tile alone did not.
+    auto load_y = [&](int64_t tile, double (&yv)[2]) {
+        const int64_t obs = obs_begin + tile * kTileRows + g1_mt * 8 + (lane >> 2);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int t = g1_nt * 8 + (lane & 3) * 2 + i;
+            yv[i] = (a.Y != nullptr && tile < ntiles && obs < obs_end && t < nt) ? a.Y[(obs * ntasks + task) * a.nt + t]
+                                                                                  : 0.0;
+        }
+    };
+    double y_cur[2], y_next[2];
+    load_y(0, y_cur);
+
     for (int64_t tile = 0; tile < ntiles; ++tile) {
         const int b = int(tile & 1);
+        load_y(tile + 1, y_next);
         const uint32_t parity = uint32_t((tile >> 1) & 1);
         long long polls = 0;
         while (!mbar_try_wait(&sm.full[b], parity)) {
@@ -193,14 +209,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
         if (g1_nt * 8 < nt) {
             const int row = g1_mt * 8 + (lane >> 2);
             const int64_t obs = base + row;
-            // this lane's two y values, loaded before the contraction so that
-            // their global-memory latency hides behind it
-            double yv[2];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int t = g1_nt * 8 + (lane & 3) * 2 + i;
-                yv[i] = (a.Y != nullptr && obs < obs_end && t < nt) ? a.Y[(obs * ntasks + task) * a.nt + t] : 0.0;
-            }
+            const double yv[2] = {y_cur[0], y_cur[1]};
             // four independent accumulator chains over k (k0 mod 16) keep the
             // tensor pipe busy instead of waiting on one dependent chain
             double dk[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
@@ -250,6 +259,8 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
         __syncthreads();  // all reads of X[b] and R done
         fence_proxy_async();
         issue(tile + 2);
+        y_cur[0] = y_next[0];
+        y_cur[1] = y_next[1];
     }
 
     // this CTA's partial: one double per (t, f)
