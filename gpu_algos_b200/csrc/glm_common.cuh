@@ -1,6 +1,8 @@
 // glm_common.cuh -- shared device/host helpers of libglm_b200.so (sm_100a).
 #pragma once
 
+#include <utility>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -147,6 +149,32 @@ __device__ __forceinline__ T finalize_value(S sum, T m, double lambda, double al
         }
     }
     return from_arith<T>(g);
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// A kernel that consumes the previous kernel's outputs is launched with
+// programmatic stream serialization (pdl_launch) and waits with
+// pdl_wait_for_producer() before its first read of them; a producer calls
+// pdl_allow_dependents() once it has started, so the consumer's launch
+// overlaps the producer's tail.  The consumer is scheduled only after every
+// producer CTA has started, so it never takes resources a producer CTA waits for.
+__device__ __forceinline__ void pdl_wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Logistic function 1 / (1 + e^-z) for the logistic link (expf / exp; an

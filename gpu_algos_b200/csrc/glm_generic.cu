@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(256)
     glm_finalize_kernel(const P* __restrict__ part, int64_t nparts, int64_t total,
                         const T* __restrict__ M, T* __restrict__ grad, double* __restrict__ partial_out,
                         double lambda, double alpha, int reg) {
+    pdl_wait_for_producer();  // the partials are the previous kernel's output
     const int lane = threadIdx.x & (kWarp - 1);
     const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
     for (int64_t e = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; e < total; e += nwarps) {
@@ -166,9 +167,10 @@ int finalize_launch(const P* part, int64_t nparts, int64_t total, const T* M, T*
     const int64_t warps_per_block = 256 / kWarp;
     const unsigned blocks = unsigned(std::max<int64_t>(
         1, std::min<int64_t>(int64_t(sm_count()) * 8, (total + warps_per_block - 1) / warps_per_block)));
-    glm_finalize_kernel<T, P><<<blocks, 256, 0, stream>>>(part, nparts, total, M, grad, partial_out,
-                                                          lambda, alpha, reg ? 1 : 0);
+    const cudaError_t e = pdl_launch(glm_finalize_kernel<T, P>, dim3(blocks), dim3(256), 0, stream, part, nparts,
+                                     total, M, grad, partial_out, lambda, alpha, reg ? 1 : 0);
     count_launch();
+    if (e != cudaSuccess) return int(e);
     return launch_status();
 }
 

@@ -90,6 +90,7 @@ __device__ __forceinline__ uint64_t* flags_of(void* base, int world, int64_t max
 template <typename T>
 __global__ void __launch_bounds__(kExThreads)
     glm_exchange_kernel(const ExArgs a, const T* __restrict__ M, T* __restrict__ grad, double* __restrict__ partial_out) {
+    pdl_wait_for_producer();  // the partials are the previous kernel's output
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = kExThreads / 32;
     const int blk = blockIdx.x, nblk = gridDim.x;
     const int64_t chunk = (a.total + nblk - 1) / nblk;
@@ -256,8 +257,10 @@ int exchange_launch(glmb_peer_group* g, const double* part, int64_t nparts, int6
              g->d_status, local_status, lambda, alpha, reg ? 1 : 0};
     // every rank derives the same block count from the same total
     const int nblk = int(std::max<int64_t>(1, std::min<int64_t>(kExMaxBlocks, (total + kExElemsPerBlock - 1) / kExElemsPerBlock)));
-    glm_exchange_kernel<T><<<nblk, kExThreads, 0, stream>>>(a, M, grad, partial_out);
+    const cudaError_t e = pdl_launch(glm_exchange_kernel<T>, dim3(nblk), dim3(kExThreads), 0, stream, a, M, grad,
+                                     partial_out);
     count_launch();
+    if (e != cudaSuccess) return int(e);
     return launch_status();
 }
 

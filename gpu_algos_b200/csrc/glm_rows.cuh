@@ -156,6 +156,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
     const T* __restrict__ Y = static_cast<const T*>(a.Y);
     T* __restrict__ Yhat = static_cast<T*>(a.Yhat);
 
+    pdl_allow_dependents();  // the reduction of this launch's partials may start launching
     const int lane = threadIdx.x & (kWarp - 1);
     const int warp = threadIdx.x >> 5;
     const int seg_log2 = FULL ? 5 : a.seg_log2;
