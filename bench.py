@@ -262,8 +262,8 @@ def run_reference(args):
     cpu_pass(pyoracle, w, X, b, Y)
     t1 = time.perf_counter() - t0
     # each step is a bounded sample: keep the whole run near a minute of CPU time
-    budget = 60.0 / max(1, args.steps + args.warmup)
-    rows = max(min(rows, 64), int(rows * min(1.0, budget / max(t1, 1e-9))))
+    cpu_seconds = 60.0 / max(1, args.steps + args.warmup)
+    rows = max(min(rows, 64), int(rows * min(1.0, cpu_seconds / max(t1, 1e-9))))
     X, Y = X[:rows], Y[:rows]
     for _ in range(args.warmup):
         cpu_pass(pyoracle, w, X, b, Y)

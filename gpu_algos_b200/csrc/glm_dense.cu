@@ -145,9 +145,9 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Bounded wait: false when the budget ran out (which sets *failed) or, with
+// Bounded wait: false when the clock limit ran out (which sets *failed) or, with
 // `failed` given, as soon as another role has failed.  Teardown waits pass
-// failed == nullptr and only give up on the budget.
+// failed == nullptr and only give up on the limit.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity, volatile int* failed) {
     const long long t0 = clock64();
     while (!mbar_test(b, parity)) {

@@ -20,7 +20,7 @@
 // Slots alternate with the call parity: a sender can be at most one call
 // ahead of a receiver still reading, so two slot sets never collide.
 //
-// Waits are bounded by a clock budget (timeout_ms at group creation): on
+// Waits are bounded by a clock limit (timeout_ms at group creation): on
 // expiry the kernel sets the group's status word, writes NaN outputs and
 // returns; the host reads the status with glmb_peer_group_status.
 #include <algorithm>

@@ -1,6 +1,6 @@
 """Parity of the sm_100a GLM kernels with the oracle, through the C ABI.
 
-Bars (BASELINE north star): max relative error <= 1e-4 for float32 and
+Bars: max relative error <= 1e-4 for float32 and
 <= 1e-11 for float64 against the oracle on the same inputs; integer types
 bit-exact; half within the reference driver's own tolerance
 2^-(11 - tol_bits) with tol_bits = 4.
