@@ -4,13 +4,16 @@
 // to 16, nfeatures up to 256, e.g. 64 tasks x 256 features x 16 targets)
 // the row-streaming kernel cannot hold nt x nf accumulators per lane.  Here
 // a CTA owns one (task, block of observations) and walks it in tiles of
-// kTileRows rows:
+// kTileRows rows, two CTAs per SM (so that one CTA's block barriers overlap
+// the other's tensor work):
 //
 //   1. the tile's X rows (nf doubles each) are brought into shared memory by
 //      cp.async.bulk copies completing on an mbarrier, two tiles in flight
 //      (the copy of tile i+1 overlaps the arithmetic of tile i);
 //   2. Yhat[rows, t] = X_tile . M_task^T on the FP64 tensor pipe
-//      (mma.sync m8n8k4 f64), r = Yhat - y written to shared memory;
+//      (mma.sync m8n8k4 f64): four 8 x 8 output blocks, each computed by two
+//      warps over the two halves of K, into shared memory (the two halves are
+//      added, and y subtracted, when step 3 reads them);
 //   3. G[t, f] += r^T . X_tile, again m8n8k4 f64, G held in registers
 //      (16 x 256 doubles over 8 warps) for the CTA's whole block.
 //
@@ -29,8 +32,9 @@ namespace glmb {
 
 namespace {
 
-constexpr int kTileRows = 32;                 // observations per tile
+constexpr int kTileRows = 16;                 // observations per tile
 constexpr int kTileThreads = 256;             // 8 warps
+constexpr int kCtasPerSm = 2;
 constexpr int kMaxF = 256;                    // features per CTA pass
 constexpr int kMaxT = 16;                     // targets
 constexpr int kXStride = kMaxF + 4;           // padded row stride (doubles): conflict-free fragments
@@ -40,9 +44,11 @@ constexpr long long kWaitLimit = 1ll << 26;   // mbarrier polls before giving up
 struct TilesSmem {
     double M[kMaxT][kXStride];
     double X[2][kTileRows][kXStride];
-    double R[kTileRows][kRStride];
+    double D[2][kTileRows][kRStride];  // step 2's two K halves of X_tile . M^T
+    double Ys[kTileRows][kRStride];    // the tile's y (zero outside the data)
     unsigned long long full[2];
 };
+static_assert(kCtasPerSm * (sizeof(TilesSmem) + 1024) <= 228 * 1024, "two CTAs per SM");
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -106,7 +112,7 @@ struct TilesArgs {
     int32_t ctas_per_task;
 };
 
-__global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const TilesArgs a) {
+__global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel(const TilesArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     TilesSmem& sm = *reinterpret_cast<TilesSmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -160,29 +166,25 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
 #pragma unroll
         for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
 
-    const int g1_mt = warp & 3;   // step 2: 8-row block of the tile
-    const int g1_nt = warp >> 2;  // step 2: 8-target block
+    // step 2: warp w computes the 8 x 8 block (rows g1_mt, targets g1_nt)
+    // over the K half khalf
+    const int g1_mt = warp & 1, g1_nt = (warp >> 1) & 1, khalf = warp >> 2;
+    const int ksplit = (kpad / 8) * 4;  // a multiple of 4 (one DMMA step)
+    const int k_lo = khalf ? ksplit : 0, k_hi = khalf ? kpad : ksplit;
+    const int row2 = g1_mt * 8 + (lane >> 2);  // this lane's row of its block
     bool failed = false;
-    // This warp's B fragments of M for step 2 (targets g1_nt*8.., all of K),
-    // held in registers for the CTA's whole block: step 2 then reads only X
-    // fragments from shared memory (one 8-byte load per DMMA instead of two).
-    double mreg[kMaxF / 4];
-    {
-        const double* mb = &sm.M[g1_nt * 8 + (lane >> 2)][lane & 3];
-#pragma unroll
-        for (int k = 0; k < kMaxF / 4; ++k) mreg[k] = mb[4 * k];
-    }
 
-    // This lane's two y values of a tile (step 2's residual), loaded one tile
-    // ahead: Y streams from DRAM, and a whole tile of work hides its latency
-    // where the contraction of one tile alone did not.
+    // This lane's two y values of a tile (K-half-0 warps own them), loaded one
+    // tile ahead: Y streams from DRAM, and a whole tile of work hides its
+    // latency where the contraction of one tile alone did not.
     auto load_y = [&](int64_t tile, double (&yv)[2]) {
-        const int64_t obs = obs_begin + tile * kTileRows + g1_mt * 8 + (lane >> 2);
+        const int64_t obs = obs_begin + tile * kTileRows + row2;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             const int t = g1_nt * 8 + (lane & 3) * 2 + i;
-            yv[i] = (a.Y != nullptr && tile < ntiles && obs < obs_end && t < nt) ? a.Y[(obs * ntasks + task) * a.nt + t]
-                                                                                  : 0.0;
+            yv[i] = (khalf == 0 && a.Y != nullptr && tile < ntiles && obs < obs_end && t < nt)
+                        ? a.Y[(obs * ntasks + task) * a.nt + t]
+                        : 0.0;
         }
     };
     double y_cur[2], y_next[2];
@@ -204,48 +206,56 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
             return;
         }
         const int64_t base = obs_begin + tile * kTileRows;
+        const int64_t obs2 = base + row2;
 
-        // step 2: yhat for an 8 x 8 (rows x targets) block per warp
-        if (g1_nt * 8 < nt) {
-            const int row = g1_mt * 8 + (lane >> 2);
-            const int64_t obs = base + row;
-            const double yv[2] = {y_cur[0], y_cur[1]};
-            // four independent accumulator chains over k (k0 mod 16) keep the
-            // tensor pipe busy instead of waiting on one dependent chain
-            double dk[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
-            const double* xa = &sm.X[b][g1_mt * 8 + (lane >> 2)][lane & 3];
+        // step 2: this warp's K half of an 8 x 8 (rows x targets) block
+        {
+            double d[2] = {0.0, 0.0};
+            if (g1_nt * 8 < nt) {
+                // four independent accumulator chains (k mod 16)
+                double dk[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
+                const double* xa = &sm.X[b][row2][lane & 3];
+                const double* mb = &sm.M[g1_nt * 8 + (lane >> 2)][lane & 3];
+                int k0 = k_lo;
+                for (; k0 + 16 <= k_hi; k0 += 16) {
 #pragma unroll
-            for (int k = 0; k < kMaxF / 4; ++k)
-                if (4 * k < kpad) dmma(dk[k & 3], xa[4 * k], mreg[k]);
-            double d[2];
+                    for (int j = 0; j < 4; ++j) dmma(dk[j], xa[k0 + 4 * j], mb[k0 + 4 * j]);
+                }
 #pragma unroll
-            for (int i = 0; i < 2; ++i) d[i] = (dk[0][i] + dk[1][i]) + (dk[2][i] + dk[3][i]);
+                for (int j = 0; j < 3; ++j)
+                    if (k0 + 4 * j < k_hi) dmma(dk[j], xa[k0 + 4 * j], mb[k0 + 4 * j]);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) d[i] = (dk[0][i] + dk[1][i]) + (dk[2][i] + dk[3][i]);
+            }
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int t = g1_nt * 8 + (lane & 3) * 2 + i;
-                double r = 0.0;
-                if (obs < obs_end && t < nt) {
-                    if (a.Yhat != nullptr) a.Yhat[(obs * ntasks + task) * a.nt + t] = d[i];
-                    r = d[i] - yv[i];
-                }
-                sm.R[row][t] = r;
+                const bool in = obs2 < obs_end && t < nt;
+                sm.D[khalf][row2][t] = in ? d[i] : 0.0;
+                if (khalf == 0) sm.Ys[row2][t] = in ? y_cur[i] : 0.0;
             }
-        } else {
-            // targets beyond nt: residual rows are zero
-            const int row = g1_mt * 8 + (lane >> 2);
-#pragma unroll
-            for (int i = 0; i < 2; ++i) sm.R[row][g1_nt * 8 + (lane & 3) * 2 + i] = 0.0;
         }
         __syncthreads();
 
-        // step 3: G[t, f] += sum_rows r[row, t] * x[row, f]
+        // predictions, when asked for: one element per thread (16 x 16)
+        if (a.Yhat != nullptr) {
+            const int r = tid >> 4, t = tid & 15;
+            const int64_t obs = base + r;
+            if (obs < obs_end && t < nt)
+                a.Yhat[(obs * ntasks + task) * a.nt + t] = sm.D[0][r][t] + sm.D[1][r][t];
+        }
+
+        // step 3: G[t, f] += sum_rows r[row, t] * x[row, f], r = (D0 + D1) - y
         const int nmt = nt > 8 ? 2 : 1;
 #pragma unroll
         for (int k0 = 0; k0 < kTileRows; k0 += 4) {
             const int kr = k0 + (lane & 3);
             double av[2], bv[4];
 #pragma unroll
-            for (int mi = 0; mi < 2; ++mi) av[mi] = sm.R[kr][mi * 8 + (lane >> 2)];
+            for (int mi = 0; mi < 2; ++mi) {
+                const int t = mi * 8 + (lane >> 2);
+                av[mi] = (sm.D[0][kr][t] + sm.D[1][kr][t]) - sm.Ys[kr][t];
+            }
 #pragma unroll
             for (int ni = 0; ni < 4; ++ni) bv[ni] = sm.X[b][kr][warp * 32 + ni * 8 + (lane >> 2)];
 #pragma unroll
@@ -256,7 +266,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) glm_tiles_f64_kernel(const Ti
                 }
             }
         }
-        __syncthreads();  // all reads of X[b] and R done
+        __syncthreads();  // all reads of X[b], D and Ys done
         fence_proxy_async();
         issue(tile + 2);
         y_cur[0] = y_next[0];
@@ -295,14 +305,14 @@ bool tiles_f64_supported(int64_t nf, int64_t nt, int64_t ntasks, const void* X) 
 
 TilesPlan tiles_f64_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
     TilesPlan p;
-    const int64_t sms = sm_count();
-    // enough CTAs for several waves of one CTA per SM, each with >= 4 tiles
+    const int64_t sms = int64_t(sm_count()) * kCtasPerSm;  // CTAs per wave
+    // enough CTAs for several waves, each with >= 4 tiles
     const int64_t want = std::max<int64_t>(1, (8 * sms + ntasks - 1) / ntasks);
     const int64_t most = std::max<int64_t>(1, nobs / (4 * kTileRows));
     int64_t cpt = std::min(want, most);
     // ... and, among CTA counts per task between want/2 and 2*want, the one
-    // whose total fills the last wave best (64 tasks: 37 per task = 16 full
-    // waves of 148, where 19 per task left the 9th wave 78 % empty)
+    // whose total fills the last wave best (64 tasks with 2 x 148 CTAs per
+    // wave: 37 per task = 8 full waves)
     {
         double best = -1.0;
         const int64_t lo = std::max<int64_t>(1, want / 2), hi = std::min(most, 2 * want);
