@@ -270,7 +270,7 @@ def test_tiles_path_multitask_f64(oracle):
 
 
 @pytest.mark.parametrize("shape", [(1, 1, 32, 9), (129, 1, 64, 16), (1000, 3, 96, 40), (4097, 1, 256, 256),
-                                   (700, 2, 4096, 12), (3000, 1, 128, 300), (257, 5, 36, 129)])
+                                   (700, 2, 4096, 12), (3000, 1, 128, 300), (257, 5, 36, 129), (500, 1, 64, 700)])
 def test_dense_path_float32(shape, oracle):
     """tcgen05 3xTF32 path (many targets): gradient, predictions, partials."""
     nobs, ntasks, nf, nt = shape
