@@ -314,6 +314,12 @@ class ClockSampler:
             if len(parts) >= 9:
                 self.samples.append((time.time(), parts))
 
+    def wait_first(self, timeout_s: float = 5.0):
+        """Block until nvidia-smi has delivered a sample (or the timeout)."""
+        t_end = time.time() + timeout_s
+        while self.proc is not None and not self.samples and time.time() < t_end:
+            time.sleep(0.02)
+
     def stop(self):
         if self.proc is not None:
             self.proc.terminate()
@@ -330,16 +336,21 @@ class ClockSampler:
                 return None
 
         window = [p for (t, p) in self.samples if t0 <= t <= t1]
+        where = "timed region"
+        if not window:  # a timed region shorter than the sampling period: the samples next to it
+            window = [p for (t, p) in self.samples if t0 - 0.5 <= t <= t1 + 0.5]
+            where = "within 0.5 s of the timed region"
         busy = [p for p in window if (num(p[2]) or 0) >= 50] or window
         if not busy:
             busy = [p for (_, p) in self.samples]
+            where = "whole run"
         if not busy:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for p in busy for i in range(4) if p[5 + i].lower().startswith("active")})
         sm = [num(p[0]) for p in busy if num(p[0]) is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": num(busy[0][1]), "reasons": reasons, "samples": len(busy),
+                "sm_max_mhz": num(busy[0][1]), "reasons": reasons, "samples": len(busy), "sampled": where,
                 "power_w_max": max((num(p[3]) or 0) for p in busy)}
 
 
@@ -554,6 +565,7 @@ def run_ours(args):
     tf32_burst, tf32_peak = measured_tf32_tflops(device) if (w.name == "dense" and rank == 0) else (None, None)
     props = torch.cuda.get_device_properties(device)
     sampler = ClockSampler(f"GPU-{props.uuid}")
+    sampler.wait_first()
 
     for _ in range(args.warmup):
         step(X, Y)
