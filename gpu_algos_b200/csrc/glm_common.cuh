@@ -151,6 +151,21 @@ __device__ __forceinline__ T finalize_value(S sum, T m, double lambda, double al
     return from_arith<T>(g);
 }
 
+// Sets a kernel's dynamic shared-memory limit once per device: the attribute
+// is per device, so a process that drives several GPUs sets it on each
+// (`done` holds one bit per device ordinal).
+template <typename F>
+inline cudaError_t set_smem_limit_once(std::atomic<uint64_t>& done, F* kernel, size_t bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t(1) << dev) : 0;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
+
 // ---- programmatic dependent launch ----------------------------------------
 // A kernel that consumes the previous kernel's outputs is launched with
 // programmatic stream serialization (pdl_launch) and waits with

@@ -646,16 +646,9 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
         return GLMB_ERR_UNSUPPORTED;
 
     const size_t smem = sizeof(DenseSmem) + 1024;
-    static bool attr = false;
-    if (!attr) {
-        if ((e = cudaFuncSetAttribute(glm_dense_gemm_kernel<kGemm1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      int(smem))) != cudaSuccess)
-            return int(e);
-        if ((e = cudaFuncSetAttribute(glm_dense_gemm_kernel<kGemm2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      int(smem))) != cudaSuccess)
-            return int(e);
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr1{0}, attr2{0};
+    if ((e = set_smem_limit_once(attr1, glm_dense_gemm_kernel<kGemm1>, smem)) != cudaSuccess) return int(e);
+    if ((e = set_smem_limit_once(attr2, glm_dense_gemm_kernel<kGemm2>, smem)) != cudaSuccess) return int(e);
     DenseArgs args{nf, nt, ntasks, nobs, p.nt_pad, p.obs_per_split, Y, Yhat, R, R_lo, P, status};
     // grids count CTAs: two per pair (the kernel's cluster shape)
     const dim3 g1(unsigned(2 * ((nobs + 2 * kBM - 1) / (2 * kBM))), unsigned((nt + kBN - 1) / kBN), unsigned(ntasks));

@@ -71,15 +71,16 @@ auto rows_kernel_for(int mode) {
 
 template <typename T, int VEC, int CPL, int NT, bool FULL>
 int rows_ctas_per_sm(int mode) {
-    // cached per instance and mode; every device this library runs on is a B200
+    using Shape = RowsShape<T, VEC, CPL, NT>;
+    const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;
+    auto kern = rows_kernel_for<T, VEC, CPL, NT, FULL>(mode);
+    // the shared-memory limit is set on every device; the occupancy is cached
+    // per instance and mode (every device this library runs on is a B200)
+    static std::atomic<uint64_t> attr[kRowsModes];
+    if (smem > 48 * 1024) set_smem_limit_once(attr[mode], kern, smem);
     static int cached[kRowsModes] = {0, 0, 0, 0, 0};
     int& c = cached[mode];
     if (c == 0) {
-        using Shape = RowsShape<T, VEC, CPL, NT>;
-        const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;
-        auto kern = rows_kernel_for<T, VEC, CPL, NT, FULL>(mode);
-        if (smem > 48 * 1024)
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         int n = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kRowsThreads, smem) != cudaSuccess)
             n = 1;

@@ -339,13 +339,9 @@ int tiles_f64_launch(const TilesPlan& p, const double* X, const double* M, const
                      double* part, int* status, int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,
                      cudaStream_t stream) {
     if (p.ctas_per_task == 0) return GLMB_OK;
-    static bool attr_set = false;
-    if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(glm_tiles_f64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   int(p.smem_bytes));
-        if (e != cudaSuccess) return int(e);
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    const cudaError_t e = set_smem_limit_once(attr, glm_tiles_f64_kernel, p.smem_bytes);
+    if (e != cudaSuccess) return int(e);
     TilesArgs a{X, M, Y, Yhat, part, status, nf, nt, ntasks, nobs, p.obs_per_cta, p.ctas_per_task};
     glm_tiles_f64_kernel<<<unsigned(int64_t(p.ctas_per_task) * ntasks), kTileThreads, p.smem_bytes, stream>>>(a);
     count_launch();
