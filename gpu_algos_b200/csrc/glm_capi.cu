@@ -123,8 +123,13 @@ size_t gradient_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
         const RowsPlan a = rows_plan<T>(nf, nt, ntasks, nobs, true, true);
         const RowsPlan b = rows_plan<T>(nf, nt, ntasks, nobs, false, true);
         all_rows = a.ok && b.ok;
-        if (a.ok) need = std::max(need, round_up(a.part_doubles * sizeof(double), 256));
-        if (b.ok) need = std::max(need, round_up(b.part_doubles * sizeof(double), 256));
+        // the CTA partials, then (glmb_gradient_loss_*) one squared-residual sum per CTA
+        auto rows_need = [&](const RowsPlan& p) {
+            return round_up(p.part_doubles * sizeof(double), 256) +
+                   round_up(size_t(ntasks) * size_t(p.ctas_per_task) * sizeof(double), 256);
+        };
+        if (a.ok) need = std::max(need, rows_need(a));
+        if (b.ok) need = std::max(need, rows_need(b));
     }
     if constexpr (std::is_same_v<T, float>) {
         if (!all_rows && dense_f32_supported(nf, nt, ntasks, std::max<int64_t>(nobs, 1), nullptr, nullptr)) {
@@ -165,11 +170,15 @@ struct PeerFinish {
 
 // With `peer` set (float/double only), the CTA partials are summed across
 // the ranks of the group by the exchange kernel instead of the local finalize.
+// With `fused_loss` set (float/double, Yhat written, one GPU), a shape that
+// the rows kernel serves also gets the objective in fused_loss[0] from the
+// same pass over X, Y and M, and *loss_done says so; other shapes leave the
+// loss to the caller.
 template <typename T>
 int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* partial_out,
                   int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, double lambda, double alpha,
                   uint32_t flags, void* ws, size_t ws_bytes, cudaStream_t stream,
-                  glmb_peer_group* peer = nullptr) {
+                  glmb_peer_group* peer = nullptr, T* fused_loss = nullptr, bool* loss_done = nullptr) {
     if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0) return GLMB_ERR_INVALID_VALUE;
     if (flags & ~(GLMB_GRAD_REGULARIZE | GLMB_GRAD_WRITE_YHAT | GLMB_GRAD_Y_ZERO | GLMB_GRAD_LOGISTIC))
         return GLMB_ERR_INVALID_VALUE;
@@ -196,15 +205,31 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
     if constexpr (kRowsKernelType<T>) {
         const RowsPlan p = rows_plan<T>(nf, nt, ntasks, nobs, aligned16(X), true);
         if (p.ok) {
-            Scratch sc(ws, ws_bytes, round_up(p.part_doubles * sizeof(double), 256), stream);
+            const bool fuse = kRowsType<T> && fused_loss != nullptr && loss_done != nullptr && write_yhat &&
+                              !logistic && peer == nullptr && partial_out == nullptr;
+            const size_t part_bytes = round_up(p.part_doubles * sizeof(double), 256);
+            const int64_t nloss = ntasks * int64_t(p.ctas_per_task);
+            Scratch sc(ws, ws_bytes, part_bytes + (fuse ? round_up(size_t(nloss) * sizeof(double), 256) : 0),
+                       stream);
             if (sc.status() != GLMB_OK) return sc.status();
+            double* loss_part = fuse ? reinterpret_cast<double*>(sc.as<char>() + part_bytes) : nullptr;
             RowsArgs a{X, M, Yin, Yhat_out, sc.as<double>(), nf, nt, ntasks, nobs, p.obs_per_cta,
-                       p.ctas_per_task, 0, p.ctas_per_task, p.seg_log2};
+                       p.ctas_per_task, 0, p.ctas_per_task, p.seg_log2, loss_part};
             set_last_path("rows");
             const int mode = logistic ? (write_yhat ? kRowsGradLogitYhat : kRowsGradLogit)
-                                      : (write_yhat ? kRowsGradYhat : kRowsGrad);
+                                      : (fuse ? kRowsGradYhatLoss : (write_yhat ? kRowsGradYhat : kRowsGrad));
             st = rows_launch<T>(p, mode, a, stream);
             if (st != GLMB_OK) return st;
+            if constexpr (kRowsType<T>) {
+                if (fuse) {
+                    st = finalize_launch<T, double>(sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M, grad,
+                                                    nullptr, lambda, alpha, reg, stream);
+                    if (st != GLMB_OK) return st;
+                    *loss_done = true;
+                    return loss_from_partials_launch<T>(loss_part, nloss, M, ntasks * nt * nf, fused_loss, lambda,
+                                                        alpha, stream);
+                }
+            }
             if constexpr (kRowsType<T>) {
                 if (peer != nullptr)
                     return exchange_launch<T>(peer, sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M, grad,
@@ -422,10 +447,11 @@ GLMB_DEFINE_BASIC(u64, uint64_t, uint64_t)
         if (flags & GLMB_GRAD_LOGISTIC) return GLMB_ERR_UNSUPPORTED; /* the loss is the squared error */ \
         return guarded([&] {                                                                       \
             const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);                         \
+            bool fused = false; /* the rows kernel summed the squared residuals */                 \
             int st = glmb::gradient_impl<T>(X, M, Y, grad_M, Yhat, nullptr, nf, nt, ntasks, nobs,  \
                                             lambda, alpha, flags | GLMB_GRAD_WRITE_YHAT, workspace, \
-                                            workspace_bytes, s);                                   \
-            if (st != GLMB_OK) return st;                                                          \
+                                            workspace_bytes, s, nullptr, loss, &fused);            \
+            if (st != GLMB_OK || fused) return st;                                                 \
             /* the gradient's scratch is free again in stream order */                             \
             return glmb::loss_launch<T>(M, (flags & GLMB_GRAD_Y_ZERO) ? nullptr : Y, Yhat, loss, nf, nt, \
                                         ntasks, nobs, lambda, alpha, workspace, workspace_bytes, s); \

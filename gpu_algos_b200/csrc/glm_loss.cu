@@ -8,6 +8,8 @@
 // over Y and Yhat (HBM-bound: 2 sizeof(T) bytes per element, grid = SMs x 4
 // CTAs, each CTA's sum to scratch), then one CTA sums the CTA partials in a
 // fixed order, adds the model terms (one pass over M) and writes the scalar.
+// When the gradient's rows kernel has already summed the squared residuals
+// (glmb_gradient_loss_*), only the second launch runs, on its partials.
 // float/double/half carry the sums in double (the reference sums in its
 // Number type; double is closer to the exact sum); integer types compute
 // modulo 2^bits in their unsigned arithmetic type, which is what the
@@ -152,6 +154,23 @@ int loss_launch(const T* M, const T* Y, const T* Yhat, T* loss, int64_t nf, int6
     count_launch();
     return launch_status();
 }
+
+template <typename T>
+int loss_from_partials_launch(const double* part, int64_t nparts, const T* M, int64_t size_M, T* loss,
+                              double lambda, double alpha, cudaStream_t stream) {
+    static_assert(std::is_same_v<typename LossAcc<T>::type, double>, "double data term");
+    if (loss == nullptr || nparts < 0 || nparts > int64_t(0x7fffffff) || (nparts > 0 && part == nullptr) ||
+        (size_M > 0 && M == nullptr))
+        return GLMB_ERR_INVALID_VALUE;
+    glm_loss_final_kernel<T, double><<<1, kFinalThreads, 0, stream>>>(part, int(nparts), M, size_M, loss, lambda,
+                                                                     alpha);
+    count_launch();
+    return launch_status();
+}
+template int loss_from_partials_launch<float>(const double*, int64_t, const float*, int64_t, float*, double, double,
+                                              cudaStream_t);
+template int loss_from_partials_launch<double>(const double*, int64_t, const double*, int64_t, double*, double,
+                                               double, cudaStream_t);
 
 #define GLMB_INSTANTIATE_LOSS(T)                                                                        \
     template int loss_launch<T>(const T*, const T*, const T*, T*, int64_t, int64_t, int64_t, int64_t, double, \

@@ -17,4 +17,12 @@ template <typename T>
 int loss_launch(const T* M, const T* Y, const T* Yhat, T* loss, int64_t nf, int64_t nt, int64_t ntasks,
                 int64_t nobs, double lambda, double alpha, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+// The same scalar from a finished data term: `part` holds `nparts` partial
+// sums of (Yhat - Y)^2 in double (the rows kernel's kRowsGradYhatLoss CTA
+// partials), summed here in order before the model terms are added.
+// float and double.
+template <typename T>
+int loss_from_partials_launch(const double* part, int64_t nparts, const T* M, int64_t size_M, T* loss,
+                              double lambda, double alpha, cudaStream_t stream);
+
 }  // namespace glmb

@@ -34,13 +34,17 @@ namespace glmb {
 // kRowsGradLogit*: logistic link -- the residual is sigmoid(x.m) - y, scaled
 // by 1/2 so that the finalize's 2*sum gives the gradient of the logistic
 // negative log-likelihood; the written prediction is sigmoid(x.m).
+// kRowsGradYhatLoss: kRowsGradYhat that also sums the squared residuals of
+// its rows (in double) into one partial per CTA, the objective's data term,
+// so the loss costs no second pass over Y and Yhat.
 enum RowsMode : int {
     kRowsGrad = 0,
     kRowsGradYhat = 1,
     kRowsPredict = 2,
     kRowsGradLogit = 3,
     kRowsGradLogitYhat = 4,
-    kRowsModes = 5
+    kRowsGradYhatLoss = 5,
+    kRowsModes = 6
 };
 
 
@@ -63,6 +67,7 @@ struct RowsArgs {
     int64_t part_offset;  // column of this launch's first CTA
     int32_t ctas_per_task;
     int32_t seg_log2;
+    double* loss_part;  // kRowsGradYhatLoss: sum of r^2 per CTA, [task][ctas_per_task]
 };
 
 template <typename T, int VEC, int CPL, int NT>
@@ -148,7 +153,9 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
     constexpr int LOG2U = Shape::LOG2U;
     constexpr bool GRAD = MODE != kRowsPredict;
     constexpr bool LOGIT = MODE == kRowsGradLogit || MODE == kRowsGradLogitYhat;
-    constexpr bool WRITE = MODE == kRowsGradYhat || MODE == kRowsPredict || MODE == kRowsGradLogitYhat;
+    constexpr bool WRITE =
+        MODE == kRowsGradYhat || MODE == kRowsPredict || MODE == kRowsGradLogitYhat || MODE == kRowsGradYhatLoss;
+    constexpr bool LOSS = MODE == kRowsGradYhatLoss;
     extern __shared__ double smem_acc[];
 
     const T* __restrict__ X = static_cast<const T*>(a.X);
@@ -187,6 +194,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
             }
 
     D acc[NT][CPL][VEC];
+    double sq = 0.0;  // LOSS: this lane's share of sum r^2
     double* wsm = smem_acc + size_t(warp) * Shape::SLOTS;
     if constexpr (GRAD) {
 #pragma unroll
@@ -294,6 +302,11 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                 }
                 if constexpr (GRAD) {
                     const D r_mine = LOGIT ? D(0.5) * (d - yb[0][t]) : d - yb[0][t];
+                    if constexpr (LOSS) {
+                        const int64_t obs = base + u_mine;
+                        if ((lane & ((32 >> LOG2U) - 1)) == 0 && t < nt && obs < obs_end)
+                            sq = fma(double(r_mine), double(r_mine), sq);
+                    }
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
                         const D r = __shfl_sync(0xffffffffu, r_mine, u << (5 - LOG2U));
@@ -322,6 +335,9 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                     }
                     if constexpr (GRAD) {
                         const D r = LOGIT ? D(0.5) * (d - yb[u][t]) : d - yb[u][t];
+                        if constexpr (LOSS) {
+                            if (ls == 0 && t < nt && obs < obs_end) sq = fma(double(r), double(r), sq);
+                        }
 #pragma unroll
                         for (int c = 0; c < CPL; ++c)
 #pragma unroll
@@ -358,6 +374,20 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
         compute(xb, yb, base);
         after_batch();
         base = next;
+    }
+    if constexpr (LOSS) {
+        // one double per CTA: lanes, then warps, in a fixed order
+        __shared__ double loss_warp[kRowsWarps];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        if (lane == 0) loss_warp[warp] = sq;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double s = 0.0;
+#pragma unroll
+            for (int w = 0; w < kRowsWarps; ++w) s += loss_warp[w];
+            a.loss_part[blockIdx.x] = s;
+        }
     }
     if constexpr (GRAD) {
         flush();

@@ -66,6 +66,9 @@ auto rows_kernel_for(int mode) {
     if (mode == kRowsGradYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradYhat, FULL>;
     if (mode == kRowsGradLogit) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradLogit, FULL>;
     if (mode == kRowsGradLogitYhat) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradLogitYhat, FULL>;
+    if constexpr (sizeof(T) >= 4) {  // the fused objective is offered for float and double
+        if (mode == kRowsGradYhatLoss) return &glm_rows_kernel<T, VEC, CPL, NT, kRowsGradYhatLoss, FULL>;
+    }
     return &glm_rows_kernel<T, VEC, CPL, NT, kRowsPredict, FULL>;
 }
 
@@ -78,7 +81,7 @@ int rows_ctas_per_sm(int mode) {
     // per instance and mode (every device this library runs on is a B200)
     static std::atomic<uint64_t> attr[kRowsModes];
     if (smem > 48 * 1024) set_smem_limit_once(attr[mode], kern, smem);
-    static int cached[kRowsModes] = {0, 0, 0, 0, 0};
+    static int cached[kRowsModes] = {};
     int& c = cached[mode];
     if (c == 0) {
         int n = 0;
@@ -157,6 +160,8 @@ RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool ve
 
 template <typename T>
 int rows_launch(const RowsPlan& p, int mode, const RowsArgs& args, cudaStream_t stream) {
+    if (mode < 0 || mode >= kRowsModes) return GLMB_ERR_INVALID_VALUE;
+    if (mode == kRowsGradYhatLoss && (sizeof(T) < 4 || args.loss_part == nullptr)) return GLMB_ERR_UNSUPPORTED;
     if (p.ctas_per_task == 0) return GLMB_OK;
     return rows_dispatch<T>(p.vec, p.cpl, p.ntmax, [&]<int VEC, int CPL, int NT>() -> int {
         using Shape = RowsShape<T, VEC, CPL, NT>;

@@ -129,7 +129,8 @@ def loss(M, Y, Yhat, lam: float = 0.0, alpha: float = 0.0, out=None, workspace=N
 def gradient_loss(X, M, Y, lam: float = 0.0, alpha: float = 0.0, regularize: bool = True,
                   yhat_out=None, out=None, loss_out=None, workspace=None, stream=None):
     """Gradient (as :func:`gradient`) and loss (as :func:`loss`, always with
-    the elastic-net term) from one call; returns (grad, loss, yhat)."""
+    the elastic-net term) from one call; returns (grad, loss, yhat).  On the
+    rows path the squared residuals are summed in the gradient's own pass."""
     sfx = SUFFIX[X.dtype]
     nf, nt, ntasks, nobs = _dims(X, M)
     _need(X, "X", (nobs, ntasks, nf), X.dtype)

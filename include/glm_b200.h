@@ -166,12 +166,15 @@ GLMB_DECLARE_LOSS(u64, uint64_t)
 
 /* ------------------------------------------------------------------------
  * Gradient and loss from one call (float32/float64): glmb_gradient_* with
- * GLMB_GRAD_WRITE_YHAT (Yhat required), then glmb_loss_* on (M, Y, Yhat)
- * with the same lambda and alpha (the loss always carries the elastic-net
- * term; `flags` governs the gradient's).  X is read once; the loss adds one
- * read of Y and Yhat.  No single reference call does both; it replaces the
- * reference's xyyhat gradient followed by its loss kernel on the `temp`
- * prediction.
+ * GLMB_GRAD_WRITE_YHAT (Yhat required) and glmb_loss_* on (M, Y, Yhat) with
+ * the same lambda and alpha (the loss always carries the elastic-net term;
+ * `flags` governs the gradient's).  X is read once.  Where the row-streaming
+ * kernel serves the shape (glmb_last_path() == "rows": at most 8 targets and
+ * short rows, up to 1024 float / 512 double features over the targets) it
+ * sums the squared residuals in the same pass, in double, and the loss costs
+ * no further read of Y or Yhat; other shapes add one read of Y and Yhat.  No single reference call does both;
+ * it replaces the reference's xyyhat gradient followed by its loss kernel on
+ * the `temp` prediction.
  * ---------------------------------------------------------------------- */
 int glmb_gradient_loss_f32(const float* X, const float* M, const float* Y, float* grad_M, float* Yhat,
                            float* loss, int64_t nfeatures, int64_t ntargets, int64_t ntasks, int64_t nobs,

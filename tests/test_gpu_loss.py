@@ -104,26 +104,40 @@ def test_loss_is_deterministic():
     assert a.tobytes() == b.tobytes()
 
 
-def _gradient_loss(X, M, Y, lam, alpha, reg=True):
+def _gradient_loss(X, M, Y, lam, alpha, reg=True, workspace=None):
     dt = X.dtype
     nobs, ntasks, nf = X.shape
     nt = M.shape[1]
-    dX, dM, dY = G.Dev(X), G.Dev(M), G.Dev(Y)
+    dX, dM = G.Dev(X), G.Dev(M)
+    dY = G.Dev(Y) if Y is not None else None
     g = G.Dev(shape=(ntasks, nt, nf), dtype=dt)
     yh = G.Dev(shape=(nobs, ntasks, nt), dtype=dt)
     loss = G.Dev(shape=(1,), dtype=dt)
-    flags = capi.GRAD_REGULARIZE if reg else 0
-    capi.call(f"glmb_gradient_loss_{G.SFX[dt]}", dX.ptr, dM.ptr, dY.ptr, g.ptr, yh.ptr, loss.ptr, nf, nt,
-              ntasks, nobs, float(lam), float(alpha), flags, None, 0, G.stream())
+    flags = (capi.GRAD_REGULARIZE if reg else 0) | (capi.GRAD_Y_ZERO if Y is None else 0)
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel())
+    capi.call(f"glmb_gradient_loss_{G.SFX[dt]}", dX.ptr, dM.ptr, dY.ptr if dY else None, g.ptr, yh.ptr,
+              loss.ptr, nf, nt, ntasks, nobs, float(lam), float(alpha), flags, ws_ptr, ws_bytes, G.stream())
     torch.cuda.synchronize()
     path = capi.last_path()
     assert g.canary_intact() and yh.canary_intact() and loss.canary_intact()
     return g.numpy(), loss.numpy()[0], yh.numpy(), path
 
 
+# On the rows path the kernel sums the squared residuals itself (each r formed
+# in the input precision, squared and summed in double): the same value as
+# glmb_loss on the written Yhat up to the rounding of r and the order of the
+# sum.  The other paths run glmb_loss's own kernels on that Yhat: identical.
+FUSED_TOL = {np.float32: 1e-6, np.float64: 1e-13}
+
+
 @pytest.mark.parametrize("dt,shape,path", [
-    (np.float32, (5000, 2, 64, 3), "rows"),
+    (np.float32, (5000, 2, 64, 3), "rows"),      # 16-lane row segments
+    (np.float32, (5000, 2, 8, 3), "rows"),       # 2-lane row segments
+    (np.float32, (5000, 2, 128, 3), "rows"),     # one row per warp
+    (np.float32, (70001, 1, 128, 1), "rows"),    # one row per warp, 8-row batches, ragged end
+    (np.float32, (3001, 3, 33, 2), "rows"),      # unaligned rows: scalar loads
     (np.float64, (5000, 2, 64, 3), "rows"),
+    (np.float64, (9999, 1, 20, 7), "rows"),
     (np.float32, (3000, 2, 128, 40), "dense"),
     (np.float64, (3000, 3, 64, 16), "tiles"),
     (np.float32, (2000, 2, 30, 12), "generic"),
@@ -136,10 +150,47 @@ def test_gradient_loss_on_every_path(dt, shape, path, oracle):
     Y = rng.normal(size=(nobs, ntasks, nt)).astype(dt)
     g, loss, yh, got_path = _gradient_loss(X, M, Y, 0.3, 0.4)
     assert got_path == path
-    # the gradient is exactly the plain call's, the loss exactly glmb_loss on the same Yhat
+    # the gradient and the prediction are exactly the plain call's
     assert np.array_equal(g, G.gradient(X, M, Y, 0.3, 0.4, reg=True))
-    assert _gpu_loss(M, Y, yh, 0.3, 0.4).tobytes() == np.asarray(loss).tobytes()
+    assert np.array_equal(yh, G.predict(X, M))
+    two_pass = _gpu_loss(M, Y, yh, 0.3, 0.4)
+    if path == "rows":
+        assert abs(float(loss) - float(two_pass)) <= FUSED_TOL[dt] * abs(float(two_pass))
+    else:
+        assert two_pass.tobytes() == np.asarray(loss).tobytes()
     # and the loss agrees with the oracle's on the oracle's own prediction
     ref = oracle.loss(M, Y, oracle.predict(X, M), 0.3, 0.4)[0]
     tol = 1e-4 if dt == np.float32 else 1e-11
     assert abs(float(loss) - float(ref)) <= tol * abs(float(ref))
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.float64])
+def test_gradient_loss_fused_edge_cases(dt, oracle):
+    dt = np.dtype(dt)
+    rng = np.random.default_rng(21)
+    nobs, ntasks, nf, nt = 4099, 2, 32, 2
+    X = rng.uniform(-1, 1, (nobs, ntasks, nf)).astype(dt)
+    M = rng.normal(size=(ntasks, nt, nf)).astype(dt)
+    Y = rng.normal(size=(nobs, ntasks, nt)).astype(dt)
+    tol = 1e-4 if dt == np.float32 else 1e-11
+    # Y absent (zeros); the gradient unregularised while the loss keeps its elastic-net term
+    g, loss, _, path = _gradient_loss(X, M, None, 0.5, 0.25, reg=False)
+    assert path == "rows"
+    assert np.array_equal(g, G.gradient(X, M, None, 0.0, 0.0, reg=False))
+    ref = oracle.loss(M, np.zeros((nobs, ntasks, nt), dt), oracle.predict(X, M), 0.5, 0.25)[0]
+    assert abs(float(loss) - float(ref)) <= tol * abs(float(ref))
+    # no observations: the model term alone, the gradient the elastic-net term alone
+    g0, loss0, _, path = _gradient_loss(X[:0], M, Y[:0], 0.5, 0.25)
+    ref0 = oracle.loss(M, Y[:0], Y[:0], 0.5, 0.25)[0]
+    assert abs(float(loss0) - float(ref0)) <= tol * abs(float(ref0))
+    assert np.array_equal(g0, G.gradient(X[:0], M, Y[:0], 0.5, 0.25, reg=True))
+    # a caller workspace of the gradient's queried size holds the loss partials too; deterministic
+    ws_bytes = getattr(capi.lib(), f"glmb_gradient_workspace_size_{G.SFX[dt]}")(nf, nt, ntasks, nobs)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    before = capi.launch_count()
+    a = _gradient_loss(X, M, Y, 0.3, 0.4, workspace=ws)
+    b = _gradient_loss(X, M, Y, 0.3, 0.4)
+    assert a[3] == "rows"
+    assert a[1].tobytes() == b[1].tobytes() and np.array_equal(a[0], b[0])
+    # fused: rows kernel, finalize, loss scalar -- three launches per call
+    assert capi.launch_count() - before == 6
