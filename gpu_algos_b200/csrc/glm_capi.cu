@@ -370,7 +370,9 @@ const char* glmb_status_string(int status) {
         case GLMB_OK: return "success";
         case GLMB_ERR_INVALID_VALUE: return "invalid argument (negative size or NULL pointer)";
         case GLMB_ERR_WORKSPACE: return "workspace smaller than required";
-        case GLMB_ERR_UNSUPPORTED: return "unsupported device (libglm_b200 carries sm_100a code only)";
+        case GLMB_ERR_UNSUPPORTED:
+            return "unsupported: no sm_100 device (libglm_b200 carries sm_100a code only), or options this entry "
+                   "point does not offer";
         case GLMB_ERR_TOO_LARGE: return "size beyond a documented limit";
         default:
             if (status > 0 && status < 1000) return cudaGetErrorString(static_cast<cudaError_t>(status));

@@ -1,5 +1,5 @@
 // glm_rows.cuh -- fused row-streaming GLM kernel for float / double / half
-// (half: float arithmetic on 16-byte loads of 8 values, half the HBM bytes
+// (half: float arithmetic on packed loads of 4 or 8 values, half the HBM bytes
 // of float per feature).
 //
 // One pass over X computes, for every row x = X[obs, task, :],
@@ -97,6 +97,10 @@ struct XRegs {
     __device__ __forceinline__ static D get(const W (&w)[N], int v) {
         return D(w[v]);
     }
+    template <typename D>
+    __device__ __forceinline__ static D get_again(const W (&w)[N], int v) {
+        return D(w[v]);
+    }
 };
 template <int VEC>
 struct XRegs<__half, VEC> {
@@ -119,6 +123,20 @@ struct XRegs<__half, VEC> {
         const uint32_t x = w[v >> 1];
         return D(__half2float(__ushort_as_half(static_cast<unsigned short>((v & 1) ? (x >> 16) : (x & 0xffffu)))));
     }
+    // The same value, converted again where the gradient loop uses it.  Left
+    // to itself the compiler keeps the dot loop's converted floats (a batch
+    // of 8 rows: 32 registers) alive across the butterfly; a conversion it
+    // cannot match with those keeps only the packed pairs alive, which takes
+    // the kernel from 104 to 80 registers and from 2 to 3 CTAs per SM.
+    template <typename D>
+    __device__ __forceinline__ static D get_again(const W (&w)[N], int v) {
+        float f;
+        if (v & 1)
+            asm("{ .reg .f16 lo, hi; mov.b32 {lo, hi}, %1; cvt.f32.f16 %0, hi; }" : "=f"(f) : "r"(w[v >> 1]));
+        else
+            asm("{ .reg .f16 lo, hi; mov.b32 {lo, hi}, %1; cvt.f32.f16 %0, lo; }" : "=f"(f) : "r"(w[v >> 1]));
+        return D(f);
+    }
 };
 template <>
 struct XRegs<__half, 1> {
@@ -127,6 +145,10 @@ struct XRegs<__half, 1> {
     __device__ __forceinline__ static void load(const __half* p, W (&w)[1]) { VecLoad<__half, 1>::load(p, w); }
     template <typename D>
     __device__ __forceinline__ static D get(const W (&w)[1], int) {
+        return D(__half2float(w[0]));
+    }
+    template <typename D>
+    __device__ __forceinline__ static D get_again(const W (&w)[1], int) {
         return D(__half2float(w[0]));
     }
 };
@@ -313,7 +335,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                         for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get<D>(xb[u][c], v), acc[t][c][v]);
+                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get_again<D>(xb[u][c], v), acc[t][c][v]);
                     }
                 }
             }
@@ -341,7 +363,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
                         for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get<D>(xb[u][c], v), acc[t][c][v]);
+                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get_again<D>(xb[u][c], v), acc[t][c][v]);
                     }
                 }
             }

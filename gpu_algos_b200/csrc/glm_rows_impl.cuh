@@ -100,12 +100,18 @@ RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool ve
     constexpr int VW = 16 / int(sizeof(T));
     p.vec = (vec_aligned && nf % VW == 0) ? VW : 1;
     if constexpr (VW == 8) {
-        // half: the widest vector that still spreads a row over a full warp
-        // (the full-warp kernel reduces a batch of rows with the transposed
-        // butterfly; a 16-lane row would take the per-segment reduction)
+        // half: a full warp per row with 16- or 8-byte loads (the full-warp
+        // kernel reduces a batch of rows with the transposed butterfly);
+        // rows too short for that take the widest vector over a narrower
+        // segment.  Measured at 2^23-2^25 rows: nfeatures 128 runs 0.90 ms
+        // with 8-byte loads over 32 lanes against 1.32 with 16-byte loads over
+        // 16 lanes; nfeatures 64 runs 1.26 ms with 16-byte loads over 8 lanes
+        // against 1.48 with 4-byte loads over 32 lanes and 2.21 with 8-byte
+        // loads over 16.
         if (vec_aligned) {
-            int v = VW;
-            while (v > 1 && (nf % v != 0 || nf / v < kWarp)) v >>= 1;
+            auto full = [&](int v) { return nf % v == 0 && nf / v >= kWarp; };
+            int v = full(VW) ? VW : (full(VW / 2) ? VW / 2 : VW);
+            while (v > 1 && nf % v != 0) v >>= 1;
             p.vec = v;
         }
     }
@@ -161,8 +167,9 @@ RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool ve
 template <typename T>
 int rows_launch(const RowsPlan& p, int mode, const RowsArgs& args, cudaStream_t stream) {
     if (mode < 0 || mode >= kRowsModes) return GLMB_ERR_INVALID_VALUE;
-    if (mode == kRowsGradYhatLoss && (sizeof(T) < 4 || args.loss_part == nullptr)) return GLMB_ERR_UNSUPPORTED;
-    if (p.ctas_per_task == 0) return GLMB_OK;
+    if (mode == kRowsGradYhatLoss && sizeof(T) < 4) return GLMB_ERR_UNSUPPORTED;
+    if (p.ctas_per_task == 0) return GLMB_OK;  // no observations: nothing to launch
+    if (mode == kRowsGradYhatLoss && args.loss_part == nullptr) return GLMB_ERR_INVALID_VALUE;
     return rows_dispatch<T>(p.vec, p.cpl, p.ntmax, [&]<int VEC, int CPL, int NT>() -> int {
         using Shape = RowsShape<T, VEC, CPL, NT>;
         const size_t smem = mode == kRowsPredict ? 0 : Shape::SMEM;

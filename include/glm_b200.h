@@ -49,7 +49,7 @@ typedef struct CUstream_st* glmb_stream_t;
 #define GLMB_OK 0
 #define GLMB_ERR_INVALID_VALUE 1001 /* negative size, NULL pointer for a non-empty tensor */
 #define GLMB_ERR_WORKSPACE 1002     /* workspace smaller than required */
-#define GLMB_ERR_UNSUPPORTED 1003   /* no device, or device is not sm_100 */
+#define GLMB_ERR_UNSUPPORTED 1003   /* no device, device is not sm_100, or options the entry point does not offer */
 #define GLMB_ERR_TOO_LARGE 1004     /* size beyond a documented limit */
 
 /* gradient flags */
