@@ -81,13 +81,14 @@ int rows_ctas_per_sm(int mode) {
     // per instance and mode (every device this library runs on is a B200)
     static std::atomic<uint64_t> attr[kRowsModes];
     if (smem > 48 * 1024) set_smem_limit_once(attr[mode], kern, smem);
-    static int cached[kRowsModes] = {};
-    int& c = cached[mode];
+    static std::atomic<int> cached[kRowsModes] = {};
+    int c = cached[mode].load(std::memory_order_relaxed);
     if (c == 0) {
         int n = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kRowsThreads, smem) != cudaSuccess)
             n = 1;
         c = std::max(1, n);
+        cached[mode].store(c, std::memory_order_relaxed);
     }
     return c;
 }
