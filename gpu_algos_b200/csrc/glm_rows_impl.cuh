@@ -23,10 +23,10 @@ constexpr bool rows_valid() {
 
 // Vectors per lane that a row shorter than a warp may take (the kernels
 // instantiated for segments of fewer than 32 lanes): one, or two for float
-// (see rows_plan).  Any longer row spans a full warp.
+// and double (see rows_plan).  Any longer row spans a full warp.
 template <typename T, int CPL>
 constexpr bool rows_short() {
-    return CPL == 1 || (CPL == 2 && sizeof(T) == 4);
+    return CPL == 1 || (CPL == 2 && sizeof(T) >= 4);
 }
 
 // Calls f.template operator()<VEC, CPL, NT>() for the runtime triple.
@@ -140,11 +140,15 @@ RowsPlan rows_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, bool ve
         }
     if (ntmax == 0) return p;
     if (ntmax * cpl * p.vec > rows_budget<T>()) return p;
-    if constexpr (sizeof(T) == 4) {
-        // float rows of 5-8 16-byte vectors: two vectors per lane over 4 lanes
-        // rather than one over 8 (half the shuffles per row); measured on 2^26
-        // rows of 32 features: 1.54 ms against 1.82
-        if (p.vec == 4 && cpl == 1 && nvec > 4 && nvec <= 8 && ntmax * 2 * p.vec <= rows_budget<T>()) cpl = 2;
+    // Rows of 5-16 16-byte vectors (float) or 9-16 (double): two vectors per
+    // lane over half the lanes (half the shuffles per row, twice the loads in
+    // flight per lane).  Measured on 8-16 GiB of X: float 32 features 1.54 ms
+    // against 1.82, 48 features 1.45 against 1.88, 64 features 1.50 against
+    // 1.90; double 32 features 1.54 against 2.02.  Half rows are better left
+    // at one vector per lane (its two-vector kernel needs 172 registers).
+    if constexpr (sizeof(T) >= 4) {
+        const int64_t lo = sizeof(T) == 4 ? 4 : 8;
+        if (p.vec == VW && cpl == 1 && nvec > lo && nvec <= 16 && ntmax * 2 * p.vec <= rows_budget<T>()) cpl = 2;
     }
     p.cpl = cpl;
     p.ntmax = ntmax;

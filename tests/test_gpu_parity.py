@@ -66,7 +66,7 @@ def test_golden_cases_through_cabi(golden, oracle):
 
 
 @pytest.mark.parametrize("dt", [np.float32, np.float64])
-@pytest.mark.parametrize("nf", [1, 3, 4, 8, 20, 24, 32, 33, 64, 100, 128, 255, 256, 512, 1000, 1025])
+@pytest.mark.parametrize("nf", [1, 3, 4, 8, 20, 24, 32, 33, 48, 60, 64, 100, 128, 255, 256, 512, 1000, 1025])
 @pytest.mark.parametrize("nt", [1, 2, 3, 8, 9])
 def test_shapes_float(dt, nf, nt, oracle):
     for (nobs, ntasks) in ((1, 1), (33, 3), (1025, 1), (4097, 2)):
