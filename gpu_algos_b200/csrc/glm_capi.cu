@@ -2,10 +2,11 @@
 //
 // Each entry point validates its arguments, picks a kernel family and
 // launches asynchronously on the caller's stream:
-//   - "rows":    fused single-pass kernel (glm_rows.cuh) for float/double
-//                when ntargets <= 8 and the per-lane accumulators fit in
-//                registers (nfeatures up to 1024 for float, 256 for double
-//                with a single target);
+//   - "rows":    fused single-pass kernel (glm_rows.cuh) for half/float/
+//                double when ntargets <= 8 and the per-lane accumulators fit
+//                in registers (with a single target and 16-byte-aligned
+//                rows nfeatures up to 1024 for half and float, 512 for
+//                double; 256 with unaligned rows);
 //   - "tiles":   float64 with up to 16 targets and 256 features that the
 //                rows kernel cannot hold in registers: shared-memory tiles
 //                filled by cp.async.bulk, both contractions on the FP64
@@ -80,7 +81,7 @@ int check_device() {
 
 template <typename T>
 constexpr bool kRowsType = std::is_same_v<T, float> || std::is_same_v<T, double>;
-// element types the fused rows kernel is built for (half: float arithmetic, 16-byte loads of 8 values)
+// element types the fused rows kernel is built for (half: float arithmetic on packed 8- or 16-byte loads)
 template <typename T>
 constexpr bool kRowsKernelType = kRowsType<T> || std::is_same_v<T, __half>;
 
