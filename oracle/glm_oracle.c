@@ -30,6 +30,7 @@
 #include <string.h>
 
 #define ORACLE_KC 256
+#define ORACLE_FT 512 /* features per tile of the accumulation loop (cache blocking only) */
 #define ORACLE_MAX_CHUNKS 64
 #define ORACLE_POWER_SAFETY 1.05
 
@@ -39,6 +40,14 @@ void oracle_set_threads(int nthreads) { g_threads = nthreads; }
 
 int oracle_get_threads(void) {
     return g_threads > 0 ? g_threads : omp_get_max_threads();
+}
+
+/* Rows of X in a cache group: about 128 KB of row data, 1 to ORACLE_KC rows
+ * (cache blocking only; no result depends on it). */
+static inline int64_t oracle_rows_per_group(int64_t row_bytes) {
+    int64_t r = row_bytes > 0 ? (int64_t)(131072 / row_bytes) : ORACLE_KC;
+    if (r < 1) r = 1;
+    return r < ORACLE_KC ? r : ORACLE_KC;
 }
 
 /* ---- binary16 helpers (gcc _Float16, round-to-nearest-even) ---- */
@@ -115,28 +124,44 @@ static inline uint16_t f2h(float f) {
         while (nchunks > 1 && (double)nchunks * (double)K * sizeof(A) > 512e6) nchunks /= 2; \
         A* part = (A*)calloc((size_t)(nchunks * K), sizeof(A));                             \
         const int nth = oracle_get_threads();                                               \
+        const int64_t sub = oracle_rows_per_group(nf * (int64_t)sizeof(T));                 \
         for (int64_t task = 0; task < ntasks; ++task) {                                     \
             const T* Mt = M + task * K;                                                     \
             _Pragma("omp parallel for num_threads(nth) schedule(dynamic, 1)")               \
             for (int64_t c = 0; c < nchunks; ++c) {                                         \
                 A* acc = part + c * K;                                                      \
                 A* tmp = (A*)malloc((size_t)K * sizeof(A));                                 \
-                A* e = (A*)malloc((size_t)nt * sizeof(A));                                  \
+                A* e = (A*)malloc((size_t)(ORACLE_KC * nt) * sizeof(A));                    \
                 for (int64_t k = 0; k < K; ++k) acc[k] = 0;                                 \
                 const int64_t b0 = c * nblocks / nchunks, b1 = (c + 1) * nblocks / nchunks; \
                 for (int64_t b = b0; b < b1; ++b) {                                         \
                     for (int64_t k = 0; k < K; ++k) tmp[k] = 0;                             \
-                    const int64_t o1 = (b + 1) * ORACLE_KC < nobs ? (b + 1) * ORACLE_KC : nobs; \
-                    for (int64_t obs = b * ORACLE_KC; obs < o1; ++obs) {                    \
-                        const T* x = X + (obs * ntasks + task) * nf;                        \
+                    const int64_t o0 = b * ORACLE_KC;                                       \
+                    const int64_t o1 = o0 + ORACLE_KC < nobs ? o0 + ORACLE_KC : nobs;       \
+                    /* residuals of the panel's rows: the panel's (M*X^T - Y^T) block, */   \
+                    /* taken in row groups of about 128 KB so that the rows of X and    */   \
+                    /* M a group uses stay cached (each dot product as above)           */   \
+                    for (int64_t s0 = o0; s0 < o1; s0 += sub) {                             \
+                        const int64_t s1 = s0 + sub < o1 ? s0 + sub : o1;                   \
                         for (int64_t t = 0; t < nt; ++t) {                                  \
-                            const A yv = Y ? LD(Y[(obs * ntasks + task) * nt + t]) : (A)0;  \
-                            e[t] = dot_##SFX(x, Mt + t * nf, nf) - yv;                      \
+                            for (int64_t obs = s0; obs < s1; ++obs) {                       \
+                                const T* x = X + (obs * ntasks + task) * nf;                \
+                                const A yv = Y ? LD(Y[(obs * ntasks + task) * nt + t]) : (A)0; \
+                                e[(obs - o0) * nt + t] = dot_##SFX(x, Mt + t * nf, nf) - yv; \
+                            }                                                               \
                         }                                                                   \
+                    }                                                                       \
+                    /* tmp[t][f] += e[obs][t] * x[obs][f], rows in ascending order for  */  \
+                    /* every element; features in tiles so that tmp's rows stay cached */   \
+                    for (int64_t f0 = 0; f0 < nf; f0 += ORACLE_FT) {                        \
+                        const int64_t f1 = f0 + ORACLE_FT < nf ? f0 + ORACLE_FT : nf;       \
                         for (int64_t t = 0; t < nt; ++t) {                                  \
                             A* row = tmp + t * nf;                                          \
-                            const A et = e[t];                                              \
-                            for (int64_t f = 0; f < nf; ++f) row[f] += et * LD(x[f]);       \
+                            for (int64_t obs = o0; obs < o1; ++obs) {                       \
+                                const T* x = X + (obs * ntasks + task) * nf;                \
+                                const A et = e[(obs - o0) * nt + t];                        \
+                                for (int64_t f = f0; f < f1; ++f) row[f] += et * LD(x[f]);  \
+                            }                                                               \
                         }                                                                   \
                     }                                                                       \
                     for (int64_t k = 0; k < K; ++k) acc[k] += tmp[k];                       \
@@ -247,14 +272,42 @@ ORACLE_DEFINE(u32, uint32_t, uint32_t, LD_U32, ST_U32, FD_U32, GT0, LT0, LT1, SI
 ORACLE_DEFINE(u64, uint64_t, uint64_t, LD_U64, ST_U64, FD_U64, GT0, LT0, LT1, SIGN_UNSIGNED, ABS_U64);
 
 /* ---- double-carried twin of the f32 gradient (error analysis) ---- */
+/* Every product and sum in double.  Rows are taken in panels of about 128 KB:
+ * the panel's rows are widened to double once, its residuals are formed with
+ * eight interleaved partial sums per dot product (float products are exact
+ * in double, so the order only moves the last bits of a double sum), and the
+ * accumulation into each chunk's gradient adds the rows in ascending order
+ * for every element, features tiled so that the rows being updated stay in
+ * cache -- the shape that makes 2^20 x 4096 x 256 a matter of seconds. */
+static inline double dot_f64_8(const double* x, const double* m, int64_t n) {
+    double p0 = 0, p1 = 0, p2 = 0, p3 = 0, p4 = 0, p5 = 0, p6 = 0, p7 = 0;
+    int64_t f = 0;
+    for (; f + 8 <= n; f += 8) {
+        p0 += x[f + 0] * m[f + 0];
+        p1 += x[f + 1] * m[f + 1];
+        p2 += x[f + 2] * m[f + 2];
+        p3 += x[f + 3] * m[f + 3];
+        p4 += x[f + 4] * m[f + 4];
+        p5 += x[f + 5] * m[f + 5];
+        p6 += x[f + 6] * m[f + 6];
+        p7 += x[f + 7] * m[f + 7];
+    }
+    double s = ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7));
+    for (; f < n; ++f) s += x[f] * m[f];
+    return s;
+}
+
 void oracle_glm_gradient_f32_acc64(const float* X, const float* M, const float* Y, double* grad,
                                    int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,
                                    double lambda, double alpha, int with_reg) {
     const int64_t K = nt * nf;
     if (K == 0) return;
     const int nth = oracle_get_threads();
+    const int64_t panel = oracle_rows_per_group(nf * (int64_t)sizeof(double));
+    double* Md = (double*)malloc((size_t)K * sizeof(double));
     for (int64_t task = 0; task < ntasks; ++task) {
         const float* Mt = M + task * K;
+        for (int64_t k = 0; k < K; ++k) Md[k] = (double)Mt[k];
         double* g = grad + task * K;
         for (int64_t k = 0; k < K; ++k) g[k] = 0.0;
         const int64_t nchunks = ORACLE_MAX_CHUNKS;
@@ -262,19 +315,34 @@ void oracle_glm_gradient_f32_acc64(const float* X, const float* M, const float* 
 #pragma omp parallel for num_threads(nth) schedule(dynamic, 1)
         for (int64_t c = 0; c < nchunks; ++c) {
             double* acc = part + c * K;
-            double* e = (double*)malloc((size_t)nt * sizeof(double));
-            const int64_t o0 = c * nobs / nchunks, o1 = (c + 1) * nobs / nchunks;
-            for (int64_t obs = o0; obs < o1; ++obs) {
-                const float* x = X + (obs * ntasks + task) * nf;
-                for (int64_t t = 0; t < nt; ++t) {
-                    double s = 0.0;
-                    for (int64_t f = 0; f < nf; ++f) s += (double)x[f] * (double)Mt[t * nf + f];
-                    e[t] = s - (Y ? (double)Y[(obs * ntasks + task) * nt + t] : 0.0);
+            double* e = (double*)malloc((size_t)(panel * nt) * sizeof(double));
+            double* xd = (double*)malloc((size_t)(panel * nf) * sizeof(double));
+            const int64_t c0 = c * nobs / nchunks, c1 = (c + 1) * nobs / nchunks;
+            for (int64_t o0 = c0; o0 < c1; o0 += panel) {
+                const int64_t np = (o0 + panel < c1 ? o0 + panel : c1) - o0;
+                for (int64_t p = 0; p < np; ++p) {
+                    const float* x = X + ((o0 + p) * ntasks + task) * nf;
+                    double* xr = xd + p * nf;
+                    for (int64_t f = 0; f < nf; ++f) xr[f] = (double)x[f];
                 }
                 for (int64_t t = 0; t < nt; ++t)
-                    for (int64_t f = 0; f < nf; ++f) acc[t * nf + f] += e[t] * (double)x[f];
+                    for (int64_t p = 0; p < np; ++p)
+                        e[p * nt + t] = dot_f64_8(xd + p * nf, Md + t * nf, nf) -
+                                        (Y ? (double)Y[((o0 + p) * ntasks + task) * nt + t] : 0.0);
+                for (int64_t f0 = 0; f0 < nf; f0 += ORACLE_FT) {
+                    const int64_t f1 = f0 + ORACLE_FT < nf ? f0 + ORACLE_FT : nf;
+                    for (int64_t t = 0; t < nt; ++t) {
+                        double* row = acc + t * nf;
+                        for (int64_t p = 0; p < np; ++p) {
+                            const double et = e[p * nt + t];
+                            const double* xr = xd + p * nf;
+                            for (int64_t f = f0; f < f1; ++f) row[f] += et * xr[f];
+                        }
+                    }
+                }
             }
             free(e);
+            free(xd);
         }
         for (int64_t k = 0; k < K; ++k) {
             double s = 0.0;
@@ -289,6 +357,7 @@ void oracle_glm_gradient_f32_acc64(const float* X, const float* M, const float* 
         }
         free(part);
     }
+    free(Md);
 }
 
 /* ---- elastic-net proximal gradient (no counterpart in the reference) ---- */
