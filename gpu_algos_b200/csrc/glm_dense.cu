@@ -16,14 +16,20 @@
 // the deeper ring: with one CTA per tile, two 96 KB stages could not hide
 // the L2 latency of the next K block behind the MMAs of the current one.
 //
-// 3xTF32 (Ootomo & Yokota, 2022): the tensor core reads the high 19 bits of
-// an fp32 word, i.e. hi = a with its low 13 bits cleared (a tf32 value); the
-// low part a - hi is exact in fp32 and is rounded to the nearest tf32 value
-// (lo, error <= 2^-22 |a|, unbiased).  Each product is hi*hi + hi*lo + lo*hi.
-// The low parts of M and R are written to global memory once (M by a small
-// kernel, R by GEMM1's epilogue) and loaded by TMA next to the fp32 words;
-// the low part of each X tile is formed in shared memory by the epilogue
-// warps while the previous stage is multiplied.
+// 3xTF32 (Ootomo & Yokota, 2022): every fp32 operand a is split into two
+// tf32 values, hi = a rounded to the nearest tf32 value and lo = a - hi
+// (exact in fp32) rounded to the nearest tf32 value (|a - hi - lo| <=
+// 2^-22 |a|); each product is hi*hi + hi*lo + lo*hi.  Rounding hi to nearest
+// matters: the tensor core reads an fp32 word's high 19 bits, and with that
+// truncated hi every lo carries the sign of its a, so the dropped lo*lo term
+// is a bias proportional to the product itself -- predictions shrink by
+// about 5e-8 of their size, which near a solution (residuals 60x smaller
+// than the predictions, summed over 2^20 observations) is several times the
+// float rounding of the host algorithm.  With hi to nearest, lo has either
+// sign and the dropped term averages out.  The split of M and R is written
+// to global memory once (M by a small kernel, R by GEMM1's epilogue) and
+// loaded by TMA; each staged X tile is split in shared memory (hi in place,
+// lo beside it) by converter warps while the previous stage is multiplied.
 //
 // Accumulation.  The tensor core rounds each accumulation toward zero, so a
 // long accumulation in TMEM drifts towards zero by about half an ulp of the
@@ -253,11 +259,15 @@ __device__ __forceinline__ void reg_after(uint32_t (&r)[16]) {
                    "+r"(r[15]));
 }
 
-__device__ __forceinline__ float tf32_low(float a) {
-    const float rest = a - __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+__device__ __forceinline__ float tf32_rn(float a) {
     uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(rest));
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(a));
     return __uint_as_float(r);
+}
+// a ~ hi + lo, both tf32 values, hi rounded to nearest (a - hi is exact in fp32)
+__device__ __forceinline__ void tf32_split(float a, float& hi, float& lo) {
+    hi = tf32_rn(a);
+    lo = tf32_rn(a - hi);
 }
 
 // Adds the K block held in TMEM buffer `buf` (this thread's row, its 128
@@ -460,14 +470,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int s = kb % kStages;
             if (!mbar_wait(&sm.full[s], uint32_t((kb / kStages) & 1), failed)) break;
             unsigned char* st = sm.stage[s];
-            const float4* src = reinterpret_cast<const float4*>(MODE == kGemm1 ? st : st + 2 * kATileBytes);
+            float4* src = reinterpret_cast<float4*>(MODE == kGemm1 ? st : st + 2 * kATileBytes);
             float4* dst =
                 reinterpret_cast<float4*>(MODE == kGemm1 ? st + kATileBytes : st + 2 * kATileBytes + kBTileBytes);
             constexpr int n4 = (MODE == kGemm1 ? kATileBytes : kBTileBytes) / 16;
 #pragma unroll 2
             for (int i = ct; i < n4; i += kConvWarps * 32) {
                 const float4 v = src[i];
-                dst[i] = make_float4(tf32_low(v.x), tf32_low(v.y), tf32_low(v.z), tf32_low(v.w));
+                float4 h, l;
+                tf32_split(v.x, h.x, l.x);
+                tf32_split(v.y, h.y, l.y);
+                tf32_split(v.z, h.z, l.z);
+                tf32_split(v.w, h.w, l.w);
+                src[i] = h;  // the swizzled positions are the same for both tiles
+                dst[i] = l;
             }
             fence_proxy_async();
             __syncwarp();
@@ -507,9 +523,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             if (in && a.Yhat != nullptr) a.Yhat[yrow + t + u] = sum[i + u];
                             r[u] = sum[i + u] - (in && a.Y != nullptr ? a.Y[yrow + t + u] : 0.0f);
                         }
-                        *reinterpret_cast<float4*>(rrow + t) = make_float4(r[0], r[1], r[2], r[3]);
-                        *reinterpret_cast<float4*>(rlrow + t) =
-                            make_float4(tf32_low(r[0]), tf32_low(r[1]), tf32_low(r[2]), tf32_low(r[3]));
+                        float4 h, l;
+                        tf32_split(r[0], h.x, l.x);
+                        tf32_split(r[1], h.y, l.y);
+                        tf32_split(r[2], h.z, l.z);
+                        tf32_split(r[3], h.w, l.w);
+                        *reinterpret_cast<float4*>(rrow + t) = h;
+                        *reinterpret_cast<float4*>(rlrow + t) = l;
                     }
                 }
             }
@@ -537,9 +557,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (tid == 0 && sm.failed) atomicExch(a.status, 1);
 }
 
-__global__ void dense_m_lo_kernel(const float* __restrict__ M, float* __restrict__ M_lo, int64_t n) {
+__global__ void dense_m_split_kernel(const float* __restrict__ M, float* __restrict__ M_hi, float* __restrict__ M_lo,
+                                     int64_t n) {
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
-        M_lo[i] = tf32_low(M[i]);
+        tf32_split(M[i], M_hi[i], M_lo[i]);
 }
 
 // grad[e] (or partial_out[e]) from sum over splits of P[s][e], in double, fixed order.
@@ -610,7 +631,7 @@ DensePlan dense_f32_plan(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
     p.r_bytes = round_up(size_t(ntasks) * nobs * p.nt_pad * 4, 256);
     p.p_bytes = round_up(size_t(p.nsplit) * total * 4, 256);
     p.mlo_bytes = round_up(total * 4, 256);
-    p.ws_bytes = 2 * p.r_bytes + p.p_bytes + p.mlo_bytes + 256;
+    p.ws_bytes = 2 * p.r_bytes + p.p_bytes + 2 * p.mlo_bytes + 256;
     return p;
 }
 
@@ -622,12 +643,14 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
     float* R_lo = reinterpret_cast<float*>(w + p.r_bytes);
     float* P = reinterpret_cast<float*>(w + 2 * p.r_bytes);
     float* M_lo = reinterpret_cast<float*>(w + 2 * p.r_bytes + p.p_bytes);
-    int* status = reinterpret_cast<int*>(w + 2 * p.r_bytes + p.p_bytes + p.mlo_bytes);
+    float* M_hi = reinterpret_cast<float*>(w + 2 * p.r_bytes + p.p_bytes + p.mlo_bytes);
+    int* status = reinterpret_cast<int*>(w + 2 * p.r_bytes + p.p_bytes + 2 * p.mlo_bytes);
     const int64_t total = ntasks * nt * nf;
     cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
     if (e != cudaSuccess) return int(e);
 
-    dense_m_lo_kernel<<<unsigned(std::min<int64_t>(4096, (total + 255) / 256)), 256, 0, stream>>>(M, M_lo, total);
+    dense_m_split_kernel<<<unsigned(std::min<int64_t>(4096, (total + 255) / 256)), 256, 0, stream>>>(M, M_hi, M_lo,
+                                                                                                      total);
     count_launch();
 
     CUtensorMap mX1, mM, mMlo, mR, mRlo, mX2;
@@ -640,7 +663,7 @@ int dense_f32_gradient(const DensePlan& p, const float* X, const float* M, const
     const uint64_t rdims[3] = {uint64_t(p.nt_pad), uint64_t(nobs), uint64_t(ntasks)};
     const uint64_t rstr[2] = {uint64_t(p.nt_pad) * 4, uint64_t(p.nt_pad * nobs) * 4};
     const uint32_t rbox[3] = {32, kBK, 1};
-    if (!make_map(&mX1, X, xdims, xstr, xbox1, false) || !make_map(&mM, M, mdims, mstr, mbox, false) ||
+    if (!make_map(&mX1, X, xdims, xstr, xbox1, false) || !make_map(&mM, M_hi, mdims, mstr, mbox, false) ||
         !make_map(&mMlo, M_lo, mdims, mstr, mbox, false) || !make_map(&mR, R, rdims, rstr, rbox, true) ||
         !make_map(&mRlo, R_lo, rdims, rstr, rbox, true) || !make_map(&mX2, X, xdims, xstr, xbox2, true))
         return GLMB_ERR_UNSUPPORTED;
