@@ -495,9 +495,8 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
 
-        # keep stdout for the one JSON line: NCCL's own messages go to stderr
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # keep stdout for the one JSON line: whatever NCCL_DEBUG asks NCCL to
+        # print (its version, INIT lines with the rank count, ...) goes to stderr
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     n_gpus = world
@@ -570,52 +569,55 @@ def run_ours(args):
     for _ in range(args.warmup):
         step(X, Y)
     torch.cuda.synchronize()
-    # One GPU, gradient workloads: the step (its 2-4 launches) is captured once
-    # into a CUDA graph and replayed, so small shapes are not bound by host
-    # launch overhead.  (The peer exchange advances a host-side epoch per call
-    # and NCCL steps are collectives: multi-GPU steps stay host-launched.)
+    # Gradient workloads on one GPU or with the peer exchange: the K timed
+    # steps (2-4 launches each) are captured into one CUDA graph and replayed
+    # once, back to back as a fit would issue them, so the per-step cost is the
+    # kernels' and not the host's launch overhead.  The exchange keeps its
+    # call number in device memory, so every step of the graph is a new
+    # exchange.  (NCCL steps are collectives issued by torch.distributed:
+    # host-launched, timed per step.)
     graph = None
-    launches_per_step = None
     host_step = step  # the public call, launched from the host (used by e2e)
-    if world == 1 and w.kind == "gradient" and not args.no_graph:
+    if w.kind == "gradient" and not args.no_graph and (world == 1 or peer is not None or not collective):
         graph = torch.cuda.CUDAGraph()
         c0 = capi.launch_count()
         with torch.cuda.graph(graph):
-            step(X, Y)
-        launches_per_step = capi.launch_count() - c0
-        graph.replay()
+            for _ in range(args.steps):
+                step(X, Y)
+        launches_per_graph = capi.launch_count() - c0
+        graph.replay()  # upload; its K steps are further warm-up
         torch.cuda.synchronize()
-
-        def step(Xs, Ys, ev=None, _g=graph):  # noqa: F811 - the captured step
-            if ev is not None:
-                ev[0].record(stream)
-            _g.replay()
-            if ev is not None:
-                ev[1].record(stream)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
 
-    kernel_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                     for _ in range(args.steps)]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     launches0 = capi.launch_count()
     t_wall0 = time.time()
-    start.record(stream)
-    for k in range(args.steps):
-        step(X, Y, kernel_events[k])
-    end.record(stream)
-    torch.cuda.synchronize()
-    t_wall1 = time.time()
-    launches = capi.launch_count() - launches0
     if graph is not None:
-        launches = launches_per_step * args.steps
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    else:
+        kernel_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                         for _ in range(args.steps)]
+        start.record(stream)
+        for k in range(args.steps):
+            step(X, Y, kernel_events[k])
+        end.record(stream)
+        torch.cuda.synchronize()
+    t_wall1 = time.time()
+    launches = launches_per_graph if graph is not None else capi.launch_count() - launches0
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     ms_total = start.elapsed_time(end)
-    kernel_ms = statistics.mean(a.elapsed_time(b) for (a, b) in kernel_events)
+    if graph is not None:
+        kernel_ms = ms_total / args.steps  # the graph holds the gradient calls and nothing else
+    else:
+        kernel_ms = statistics.mean(a.elapsed_time(b) for (a, b) in kernel_events)
     t = torch.tensor([ms_total, kernel_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -724,7 +726,8 @@ def run_ours(args):
                 "scaling": "strong" if w.shard != "replica" else "weak", "vs_baseline": None,
                 "dtype": w.dtype, "data": "synthetic", "config": workload_config(w, n_gpus, args.exchange),
                 "roofline": roofline, "gpu_launches": int(launches), "clocks": clocks,
-                "step_launch": "CUDA graph replay of the captured call" if graph is not None else "host launches"}
+                "step_launch": (f"the {args.steps} timed calls captured in one CUDA graph, replayed once"
+                                if graph is not None else "host launches")}
         if w.kind == "fit":
             line["fit"] = {"passes_per_step": passes, "ms_per_pass": ms_per_step / passes,
                            "lipschitz": float(lip[0].item()), "nonzero": int((beta_fit != 0).sum().item())}

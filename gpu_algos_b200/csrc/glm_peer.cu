@@ -5,6 +5,9 @@
 //   slots[2][world][max_elems] doubles   (double-buffered by call parity)
 //   flags[world][kExMaxBlocks] uint64     (last call number received, per
 //                                          sender and per exchange block)
+//   ctl[2] uint64                         (this rank's completed calls and
+//                                          the exchange blocks' ticket; read
+//                                          and written by this rank only)
 // A sharded evaluation is two launches per rank:
 //   1. the usual CTA-partial kernel over the local observations
 //      (glm_rows_kernel / glm_tiles_f64_kernel / the generic pair);
@@ -18,7 +21,11 @@
 //      every rank obtains bit-identical results -- and applies the
 //      elastic-net finalize (or writes the summed partial for the optimizer).
 // Slots alternate with the call parity: a sender can be at most one call
-// ahead of a receiver still reading, so two slot sets never collide.
+// ahead of a receiver still reading, so two slot sets never collide.  The
+// call number lives in device memory (ctl[0]): every block of a call reads
+// it when it starts and the last block to finish advances it, so a call
+// captured in a CUDA graph and replayed exchanges under a new number each
+// time, exactly like a call launched from the host.
 //
 // Waits are bounded by a clock limit (timeout_ms at group creation): on
 // expiry the kernel sets the group's status word, writes NaN outputs and
@@ -40,7 +47,6 @@ struct glmb_peer_group {
     bool opened[GLMB_PEER_MAX_WORLD];  // pointer came from cudaIpcOpenMemHandle
     void** d_peers = nullptr;          // device copy of peers[]
     int* d_status = nullptr;
-    uint64_t epoch = 0;
     long long timeout_cycles = 0;
     bool connected = false;
 };
@@ -71,7 +77,6 @@ struct ExArgs {
     int64_t nparts, total, max_elems;
     void* const* peers;  // device array: base pointer of every rank's buffer
     int rank, world;
-    uint64_t epoch;
     long long timeout_cycles;
     int* status;
     const int* local_status;  // the partial kernel's own status word, or NULL
@@ -86,6 +91,33 @@ __device__ __forceinline__ uint64_t* flags_of(void* base, int world, int64_t max
     return reinterpret_cast<uint64_t*>(static_cast<double*>(base) + 2 * int64_t(world) * max_elems) +
            int64_t(sender) * kExMaxBlocks + block;
 }
+// ctl[0]: calls this rank has completed; ctl[1]: blocks of the current call done
+__device__ __forceinline__ unsigned long long* ctl_of(void* base, int world, int64_t max_elems) {
+    return reinterpret_cast<unsigned long long*>(flags_of(base, world, max_elems, world, 0));
+}
+
+// The call number every block of this launch exchanges under (ctl[0] + 1).
+__device__ __forceinline__ uint64_t call_epoch(void* own, int world, int64_t max_elems) {
+    __shared__ uint64_t s_epoch;
+    if (threadIdx.x == 0) s_epoch = __ldcg(ctl_of(own, world, max_elems)) + 1;
+    __syncthreads();
+    return s_epoch;
+}
+
+// Called by every block of the launch once its last access to the buffers
+// is issued: the last one to arrive records the call as completed.
+__device__ __forceinline__ void call_done(void* own, int world, int64_t max_elems, uint64_t epoch, int nblocks) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long* ctl = ctl_of(own, world, max_elems);
+        __threadfence();
+        if (atomicAdd(&ctl[1], 1ull) == static_cast<unsigned long long>(nblocks - 1)) {
+            ctl[1] = 0;
+            ctl[0] = epoch;
+            __threadfence();
+        }
+    }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kExThreads)
@@ -95,8 +127,9 @@ __global__ void __launch_bounds__(kExThreads)
     const int blk = blockIdx.x, nblk = gridDim.x;
     const int64_t chunk = (a.total + nblk - 1) / nblk;
     const int64_t lo = min(a.total, int64_t(blk) * chunk), hi = min(a.total, lo + chunk);
-    const int parity = int(a.epoch & 1);
     void* own = a.peers[a.rank];
+    const uint64_t epoch = call_epoch(own, a.world, a.max_elems);
+    const int parity = int(epoch & 1);
     double* mine = slot_of(own, parity, a.rank, a.world, a.max_elems);
 
     // 1. this rank's partial for the block's elements: fixed-order sum of the CTA partials
@@ -118,14 +151,14 @@ __global__ void __launch_bounds__(kExThreads)
     }
     __threadfence_system();
     __syncthreads();
-    if (tid < a.world) st_release_sys(flags_of(a.peers[tid], a.world, a.max_elems, a.rank, blk), a.epoch);
+    if (tid < a.world) st_release_sys(flags_of(a.peers[tid], a.world, a.max_elems, a.rank, blk), epoch);
 
     // 3. wait until every sender's chunk of this call has arrived (bounded)
     bool failed = false;
     if (tid < a.world) {
         const uint64_t* f = flags_of(own, a.world, a.max_elems, tid, blk);
         const long long t0 = clock64();
-        while (ld_acquire_sys(f) < a.epoch) {
+        while (ld_acquire_sys(f) < epoch) {
             if (clock64() - t0 > a.timeout_cycles) {
                 failed = true;
                 break;
@@ -142,6 +175,7 @@ __global__ void __launch_bounds__(kExThreads)
             if (partial_out != nullptr) partial_out[e] = nan;
             else grad[e] = T(nan);
         }
+        call_done(own, a.world, a.max_elems, epoch, nblk);
         return;
     }
     // every thread acquires the flags it depends on before reading the slots
@@ -150,10 +184,11 @@ __global__ void __launch_bounds__(kExThreads)
     // 4. the same rank-ordered sum on every rank, then finalize
     for (int64_t e = lo + tid; e < hi; e += kExThreads) {
         double s = 0.0;
-        for (int r = 0; r < a.world; ++r) s += slot_of(own, parity, r, a.world, a.max_elems)[e];
+        for (int r = 0; r < a.world; ++r) s += __ldcg(slot_of(own, parity, r, a.world, a.max_elems) + e);
         if (partial_out != nullptr) partial_out[e] = s;
         else grad[e] = finalize_value<T>(s, M[e], a.lambda, a.alpha, a.reg != 0);
     }
+    call_done(own, a.world, a.max_elems, epoch, nblk);
 }
 
 }  // namespace
@@ -177,7 +212,8 @@ int peer_group_create(int rank, int world, int64_t max_elems, double timeout_ms,
     int clock_khz = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, g->device);
     g->timeout_cycles = static_cast<long long>(timeout_ms * double(clock_khz > 0 ? clock_khz : 2000000));
-    g->bytes = size_t(2) * world * max_elems * sizeof(double) + size_t(world) * glmb::kExMaxBlocks * sizeof(uint64_t);
+    g->bytes = size_t(2) * world * max_elems * sizeof(double) + size_t(world) * glmb::kExMaxBlocks * sizeof(uint64_t) +
+               2 * sizeof(uint64_t);
     if (e == cudaSuccess) e = cudaMalloc(&g->buf, g->bytes);
     if (e == cudaSuccess) e = cudaMemset(g->buf, 0, g->bytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&g->d_peers), sizeof(void*) * GLMB_PEER_MAX_WORLD);
@@ -252,8 +288,7 @@ int exchange_launch(glmb_peer_group* g, const double* part, int64_t nparts, int6
     if (total > g->max_elems) return GLMB_ERR_TOO_LARGE;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != g->device) return GLMB_ERR_INVALID_VALUE;
-    ++g->epoch;
-    ExArgs a{part, nparts, total, g->max_elems, g->d_peers, g->rank, g->world, g->epoch, g->timeout_cycles,
+    ExArgs a{part, nparts, total, g->max_elems, g->d_peers, g->rank, g->world, g->timeout_cycles,
              g->d_status, local_status, lambda, alpha, reg ? 1 : 0};
     // every rank derives the same block count from the same total
     const int nblk = int(std::max<int64_t>(1, std::min<int64_t>(kExMaxBlocks, (total + kExElemsPerBlock - 1) / kExElemsPerBlock)));
