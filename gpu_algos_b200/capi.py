@@ -19,6 +19,11 @@ GLMB_ERR_INVALID_VALUE = 1001
 GLMB_ERR_WORKSPACE = 1002
 GLMB_ERR_UNSUPPORTED = 1003
 GLMB_ERR_TOO_LARGE = 1004
+GLMB_ERR_COLLECTIVE = 1005
+GLMB_ERR_PEER_TIMEOUT = 1006
+
+MG_PEER = 0
+MG_NCCL = 1
 
 PEER_HANDLE_BYTES = 64
 
@@ -103,6 +108,23 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"glmb_gradient_sharded_{s}")
         f.argtypes = [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P, _P, _SZ, _P]
         f.restype = _INT
+        f = getattr(L, f"glmb_fit_elastic_net_sharded_{s}")
+        f.argtypes = [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _INT, _INT, _U64, _P, _P, _SZ, _P]
+        f.restype = _INT
+        _PP = ctypes.POINTER(ctypes.c_void_p)
+        f = getattr(L, f"glmb_mg_gradient_{s}")
+        f.argtypes = [_P, _PP, _PP, _PP, _PP, ctypes.POINTER(_I64), _I64, _I64, _I64, _D, _D, _U32]
+        f.restype = _INT
+        f = getattr(L, f"glmb_mg_fit_elastic_net_{s}")
+        f.argtypes = [_P, _PP, _PP, _PP, _PP, ctypes.POINTER(_I64), _I64, _I64, _I64, _D, _D, _INT, _INT, _U64]
+        f.restype = _INT
+    L.glmb_mg_create.argtypes = [_INT, ctypes.POINTER(_INT), _I64, _D, _U32, ctypes.POINTER(ctypes.c_void_p)]
+    L.glmb_mg_destroy.argtypes = [_P]
+    L.glmb_mg_size.argtypes = [_P]
+    L.glmb_mg_stream.argtypes = [_P, _INT, ctypes.POINTER(ctypes.c_void_p)]
+    L.glmb_mg_synchronize.argtypes = [_P]
+    for name in ("glmb_mg_create", "glmb_mg_destroy", "glmb_mg_size", "glmb_mg_stream", "glmb_mg_synchronize"):
+        getattr(L, name).restype = _INT
 
 
 def lib() -> ctypes.CDLL:
@@ -160,4 +182,8 @@ def exported_symbols() -> list[str]:
     names += ["glmb_peer_group_create", "glmb_peer_group_connect", "glmb_peer_group_connect_local",
               "glmb_peer_group_buffer", "glmb_peer_group_status", "glmb_peer_group_destroy"]
     names += [f"glmb_gradient_sharded_{s}" for s in FLOATING]
+    names += [f"glmb_fit_elastic_net_sharded_{s}" for s in FLOATING]
+    names += ["glmb_mg_create", "glmb_mg_destroy", "glmb_mg_size", "glmb_mg_stream", "glmb_mg_synchronize"]
+    for s in FLOATING:
+        names += [f"glmb_mg_gradient_{s}", f"glmb_mg_fit_elastic_net_{s}"]
     return names

@@ -303,10 +303,13 @@ size_t fit_ws_impl(int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs) {
     return grad_ws + part + v + norm;
 }
 
+// The whole fit on one GPU, or -- with `group` -- on this rank's block of
+// observations, every partial sum completed over the group's ranks by the
+// exchange kernel (so every rank holds the same L and beta throughout).
 template <typename T>
 int fit_impl(const T* X, const T* Y, T* beta, double* lipschitz, int64_t nf, int64_t nt,
              int64_t ntasks, int64_t nobs, double lambda1, double lambda2, int n_power, int n_iter,
-             uint64_t seed, void* ws, size_t ws_bytes, cudaStream_t stream) {
+             uint64_t seed, void* ws, size_t ws_bytes, cudaStream_t stream, glmb_peer_group* group = nullptr) {
     if (nf < 0 || nt < 0 || ntasks < 0 || nobs < 0 || n_power < 0 || n_iter < 0)
         return GLMB_ERR_INVALID_VALUE;
     if (lambda1 < 0 || lambda2 < 0) return GLMB_ERR_INVALID_VALUE;
@@ -330,7 +333,7 @@ int fit_impl(const T* X, const T* Y, T* beta, double* lipschitz, int64_t nf, int
     if ((st = power_init<T>(v, nf, ntasks, seed, stream)) != GLMB_OK) return st;
     for (int it = 0; it < n_power; ++it) {
         st = gradient_impl<T>(X, v, nullptr, nullptr, nullptr, part, nf, 1, ntasks, nobs, 0.0, 0.0,
-                              GLMB_GRAD_Y_ZERO, gws, grad_ws, stream);
+                              GLMB_GRAD_Y_ZERO, gws, grad_ws, stream, group);
         if (st != GLMB_OK) return st;
         if ((st = power_step<T>(part, v, norm, lipschitz, nf, ntasks, lambda2, stream)) != GLMB_OK)
             return st;
@@ -339,7 +342,7 @@ int fit_impl(const T* X, const T* Y, T* beta, double* lipschitz, int64_t nf, int
     if (e != cudaSuccess) return int(e);
     for (int it = 0; it < n_iter; ++it) {
         st = gradient_impl<T>(X, beta, Y, nullptr, nullptr, part, nf, nt, ntasks, nobs, 0.0, 0.0, 0u,
-                              gws, grad_ws, stream);
+                              gws, grad_ws, stream, group);
         if (st != GLMB_OK) return st;
         if ((st = prox_update<T>(part, beta, lipschitz, K, ntasks, lambda1, lambda2, stream)) != GLMB_OK)
             return st;
@@ -358,6 +361,24 @@ int guarded(F&& f) {
 }
 
 }  // namespace
+
+// Entry points for the single-process multi-GPU context (glm_mg.cu).
+template <typename T>
+int sharded_gradient(const T* X, const T* M, const T* Y, T* grad, double* partial_out, int64_t nf, int64_t nt,
+                     int64_t ntasks, int64_t nobs, double lambda, double alpha, uint32_t flags,
+                     cudaStream_t stream, glmb_peer_group* group) {
+    return guarded([&] {
+        return gradient_impl<T>(X, M, Y, partial_out ? nullptr : grad, nullptr, partial_out, nf, nt, ntasks, nobs,
+                                lambda, alpha, flags, nullptr, 0, stream, group);
+    });
+}
+template int sharded_gradient<float>(const float*, const float*, const float*, float*, double*, int64_t, int64_t,
+                                     int64_t, int64_t, double, double, uint32_t, cudaStream_t, glmb_peer_group*);
+template int sharded_gradient<double>(const double*, const double*, const double*, double*, double*, int64_t,
+                                      int64_t, int64_t, int64_t, double, double, uint32_t, cudaStream_t,
+                                      glmb_peer_group*);
+int device_check() { return check_device(); }
+
 }  // namespace glmb
 
 using glmb::guarded;
@@ -375,6 +396,8 @@ const char* glmb_status_string(int status) {
             return "unsupported: no sm_100 device (libglm_b200 carries sm_100a code only), or options this entry "
                    "point does not offer";
         case GLMB_ERR_TOO_LARGE: return "size beyond a documented limit";
+        case GLMB_ERR_COLLECTIVE: return "NCCL could not be loaded, or an NCCL call failed";
+        case GLMB_ERR_PEER_TIMEOUT: return "a wait for a peer's partial ran out (that call's outputs are NaN)";
         default:
             if (status > 0 && status < 1000) return cudaGetErrorString(static_cast<cudaError_t>(status));
             return "unknown status";
@@ -570,6 +593,24 @@ int glmb_peer_group_status(glmb_peer_group* group, int* status, int reset) {
 int glmb_peer_group_destroy(glmb_peer_group* group) {
     return guarded([&] { return glmb::peer_group_destroy(group); });
 }
+
+#define GLMB_DEFINE_SHARDED_FIT(SFX, T)                                                             \
+    int glmb_fit_elastic_net_sharded_##SFX(const T* X, const T* Y, T* beta, double* lipschitz,     \
+                                           int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs,    \
+                                           double lambda1, double lambda2, int n_power, int n_iter, \
+                                           uint64_t seed, glmb_peer_group* group, void* workspace,  \
+                                           size_t workspace_bytes, glmb_stream_t stream) {          \
+        if (group == nullptr) return GLMB_ERR_INVALID_VALUE;                                        \
+        if (ntasks > 0x7fffffff) return GLMB_ERR_TOO_LARGE;                                         \
+        return guarded([&] {                                                                        \
+            return glmb::fit_impl<T>(X, Y, beta, lipschitz, nf, nt, ntasks, nobs, lambda1, lambda2, \
+                                     n_power, n_iter, seed, workspace, workspace_bytes,             \
+                                     reinterpret_cast<cudaStream_t>(stream), group);               \
+        });                                                                                         \
+    }
+
+GLMB_DEFINE_SHARDED_FIT(f32, float)
+GLMB_DEFINE_SHARDED_FIT(f64, double)
 
 #define GLMB_DEFINE_PEER(SFX, T)                                                                    \
     int glmb_gradient_sharded_##SFX(const T* X, const T* M, const T* Y, T* grad_M, double* partial_out, \

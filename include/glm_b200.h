@@ -51,6 +51,8 @@ typedef struct CUstream_st* glmb_stream_t;
 #define GLMB_ERR_WORKSPACE 1002     /* workspace smaller than required */
 #define GLMB_ERR_UNSUPPORTED 1003   /* no device, device is not sm_100, or options the entry point does not offer */
 #define GLMB_ERR_TOO_LARGE 1004     /* size beyond a documented limit */
+#define GLMB_ERR_COLLECTIVE 1005    /* NCCL could not be loaded, or an NCCL call failed */
+#define GLMB_ERR_PEER_TIMEOUT 1006  /* a wait for a peer's partial ran out (that call's outputs are NaN) */
 
 /* gradient flags */
 #define GLMB_GRAD_REGULARIZE 0x1u /* add lambda*(alpha*sign(M) + 2*(1-alpha)*M)   */
@@ -311,6 +313,86 @@ GLMB_DECLARE_PEER(f64, double)
 
 GLMB_DECLARE_FIT(f32, float)
 GLMB_DECLARE_FIT(f64, double)
+
+/* ------------------------------------------------------------------------
+ * Sharded elastic-net fit over a peer-exchange group (one call per rank,
+ * every rank with its own block of observations, the same seed and the same
+ * arguments otherwise): glmb_fit_elastic_net_* in which every power
+ * iteration and ISTA step sums its partial over the group's ranks with the
+ * exchange kernel, so every rank ends with the same beta and L.  No
+ * counterpart in the reference (single-GPU, no optimizer).  Workspace: the
+ * size glmb_fit_workspace_size_* reports for the rank's own nobs.
+ * ---------------------------------------------------------------------- */
+#define GLMB_DECLARE_SHARDED_FIT(SFX, T)                                                \
+    int glmb_fit_elastic_net_sharded_##SFX(const T* X, const T* Y, T* beta,             \
+                                           double* lipschitz, int64_t nfeatures,        \
+                                           int64_t ntargets, int64_t ntasks,            \
+                                           int64_t nobs, double lambda1, double lambda2, \
+                                           int n_power, int n_iter, uint64_t seed,      \
+                                           glmb_peer_group* group, void* workspace,     \
+                                           size_t workspace_bytes, glmb_stream_t stream);
+
+GLMB_DECLARE_SHARDED_FIT(f32, float)
+GLMB_DECLARE_SHARDED_FIT(f64, double)
+
+/* ------------------------------------------------------------------------
+ * Single-process multi-GPU context, for C and C++ hosts that drive several
+ * GPUs from one thread.  It generalises the reference's one-GPU call
+ * (Glm_gradient_xyyhat_kernel::run_device_kernel,
+ * include/cuda/kernels/glm/glm_gradient_xyyhat.cuh:642) to observations
+ * split into one contiguous block per device; the reference has no
+ * multi-GPU path, so these calls have no counterpart there.
+ *
+ * glmb_mg_create     devices[0..ndev) (distinct ordinals), one stream per
+ *                    device created here, and the exchange:
+ *                      GLMB_MG_PEER  the library's exchange kernel over
+ *                                    NVLink peer memory (enables CUDA peer
+ *                                    access between the devices);
+ *                      GLMB_MG_NCCL  ncclAllReduce, one communicator per
+ *                                    device (ncclCommInitAll); NCCL is
+ *                                    loaded from libnccl.so.2 at this call
+ *                                    (GLMB_ERR_UNSUPPORTED if absent).
+ *                    max_elems bounds nfeatures*ntargets*ntasks;
+ *                    timeout_ms bounds every peer wait.
+ * glmb_mg_gradient   X[i], Y[i]: device i's block (nobs[i] observations,
+ *                    Tensor3D layout), M[i]: a copy of the model on device
+ *                    i, grad_M[i]: the full-data gradient on device i
+ *                    (identical bits on every device).  Flags:
+ *                    GLMB_GRAD_REGULARIZE, GLMB_GRAD_Y_ZERO (Y may be NULL),
+ *                    GLMB_GRAD_LOGISTIC.
+ * glmb_mg_fit_elastic_net   the sharded ISTA fit of glmb_fit_elastic_net_*,
+ *                    beta[i] and lipschitz[i] (ntasks doubles) on device i.
+ * Calls are asynchronous on the context's streams (glmb_mg_stream) and
+ * restore the caller's current device; glmb_mg_synchronize waits for all
+ * devices and returns GLMB_ERR_PEER_TIMEOUT if an exchange wait ran out.
+ * A context is used by one host thread at a time.
+ * ---------------------------------------------------------------------- */
+#define GLMB_MG_MAX_DEVICES 64
+#define GLMB_MG_PEER 0u
+#define GLMB_MG_NCCL 1u
+typedef struct glmb_mg glmb_mg;
+
+int glmb_mg_create(int ndev, const int* devices, int64_t max_elems, double timeout_ms, uint32_t mode,
+                   glmb_mg** mg);
+int glmb_mg_destroy(glmb_mg* mg);
+int glmb_mg_size(glmb_mg* mg);
+int glmb_mg_stream(glmb_mg* mg, int i, glmb_stream_t* stream);
+int glmb_mg_synchronize(glmb_mg* mg);
+
+#define GLMB_DECLARE_MG(SFX, T)                                                         \
+    int glmb_mg_gradient_##SFX(glmb_mg* mg, const T* const* X, const T* const* M,       \
+                               const T* const* Y, T* const* grad_M, const int64_t* nobs, \
+                               int64_t nfeatures, int64_t ntargets, int64_t ntasks,     \
+                               double lambda, double alpha, uint32_t flags);            \
+    int glmb_mg_fit_elastic_net_##SFX(glmb_mg* mg, const T* const* X, const T* const* Y, \
+                                      T* const* beta, double* const* lipschitz,         \
+                                      const int64_t* nobs, int64_t nfeatures,           \
+                                      int64_t ntargets, int64_t ntasks, double lambda1, \
+                                      double lambda2, int n_power, int n_iter,          \
+                                      uint64_t seed);
+
+GLMB_DECLARE_MG(f32, float)
+GLMB_DECLARE_MG(f64, double)
 
 #ifdef __cplusplus
 }

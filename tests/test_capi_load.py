@@ -29,7 +29,9 @@ def _exported():
 def test_library_loads_and_exports_every_declared_symbol():
     L = capi.lib()
     declared = _declared_functions()
-    assert len(declared) == 4 + 4 * 11 + 9 * 2 + 1 + 6 + 2
+    # basics, per-type entry points, floating-point entry points, the no-allocation
+    # entry point, the peer group, sharded gradient and fit, the multi-GPU context
+    assert len(declared) == 4 + 4 * 11 + 9 * 2 + 1 + 6 + 2 + 2 + 5 + 2 * 2
     exported = _exported()
     missing = [n for n in declared if n not in exported]
     assert not missing, missing
@@ -50,6 +52,8 @@ def test_status_strings():
     assert "workspace" in capi.status_string(capi.GLMB_ERR_WORKSPACE)
     assert "invalid" in capi.status_string(capi.GLMB_ERR_INVALID_VALUE)
     assert "sm_100a" in capi.status_string(capi.GLMB_ERR_UNSUPPORTED)
+    assert "NCCL" in capi.status_string(capi.GLMB_ERR_COLLECTIVE)
+    assert "peer" in capi.status_string(capi.GLMB_ERR_PEER_TIMEOUT)
 
 
 def test_argument_validation_happens_before_any_device_call():
@@ -67,6 +71,17 @@ def test_argument_validation_happens_before_any_device_call():
     # empty problems are successful no-ops
     assert L.glmb_predict_f32(None, None, None, 8, 0, 1, 5, None) == 0
     assert L.glmb_gradient_u8(None, None, None, None, None, 8, 1, 0, 5, 0.0, 0.0, 0, None, 0, None) == 0
+    # the multi-GPU context checks its arguments before any device is touched
+    import ctypes
+    mg = ctypes.c_void_p()
+    devs = (ctypes.c_int * 2)(0, 0)
+    assert L.glmb_mg_create(2, devs, 16, 100.0, capi.MG_PEER, ctypes.byref(mg)) == 1001  # a device twice
+    assert L.glmb_mg_create(0, devs, 16, 100.0, capi.MG_PEER, ctypes.byref(mg)) == 1001
+    assert L.glmb_mg_create(1, devs, 16, 100.0, 7, ctypes.byref(mg)) == 1001
+    assert L.glmb_mg_synchronize(None) == 1001 and L.glmb_mg_size(None) == 0
+    assert L.glmb_mg_destroy(None) == 0
+    assert L.glmb_fit_elastic_net_sharded_f32(None, None, None, None, 4, 1, 1, 8, 0.0, 0.0, 1, 1, 0, None, None, 0,
+                                              None) == 1001
     assert capi.launch_count() == before
 
 
