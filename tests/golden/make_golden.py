@@ -1,8 +1,9 @@
 """Generate the committed golden fixtures ``tests/golden/glm_golden.npz``.
 
-Run once, in a container where the reference checkout is mounted::
+Run once, where a checkout of the reference is available, giving its root
+as the argument (or in GPU_ALGOS_REFERENCE)::
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path-to-gpu_algos-checkout>
 
 Source of truth.  The reference's CPU product goes through Eigen, which is
 absent from this image, so its C++ host path cannot be run here.  The
@@ -159,4 +160,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GPU_ALGOS_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden.py <path-to-gpu_algos-checkout>  (or set GPU_ALGOS_REFERENCE)")
+    main(root)
