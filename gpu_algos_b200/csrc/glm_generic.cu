@@ -29,16 +29,41 @@ __global__ void __launch_bounds__(256)
         const int64_t task = row % ntasks;
         const T* x = X + row * nf;
         const T* m = M + (task * nt + t) * nf;
-        D d = D(0);
-        for (int64_t f = 0; f < nf; ++f) d += to_arith<D>(m[f]) * to_arith<D>(x[f]);
         if constexpr (std::is_floating_point_v<D>) {
+            // one dot product per output, as accurate as the output type can
+            // hold: float products are exact in double; double uses the
+            // compensated dot product (error-free product and sum of every
+            // term, Ogita, Rump & Oishi 2005), so the result is as if carried
+            // in twice the working precision
+            double d;
+            if constexpr (std::is_same_v<D, double>) {
+                double s = 0.0, c = 0.0;
+                for (int64_t f = 0; f < nf; ++f) {
+                    const double a = to_arith<double>(m[f]), b = to_arith<double>(x[f]);
+                    const double p = a * b;
+                    const double ep = fma(a, b, -p);
+                    const double u = s + p;
+                    const double z = u - s;
+                    const double es = (s - (u - z)) + (p - z);
+                    s = u;
+                    c += ep + es;
+                }
+                d = s + c;
+            } else {
+                d = 0.0;
+                for (int64_t f = 0; f < nf; ++f) d = fma(to_arith<double>(m[f]), to_arith<double>(x[f]), d);
+            }
             if (logistic) d = sigmoid(d);
-        }
-        if (Yhat != nullptr) Yhat[i] = from_arith<T>(d);
-        if (E != nullptr) {
-            const D e = d - (Y != nullptr ? to_arith<D>(Y[i]) : D(0));
-            if constexpr (std::is_floating_point_v<D>) E[i] = logistic ? D(0.5) * e : e;
-            else E[i] = e;
+            if (Yhat != nullptr) Yhat[i] = from_arith<T>(D(d));
+            if (E != nullptr) {
+                const double e = d - (Y != nullptr ? to_arith<double>(Y[i]) : 0.0);
+                E[i] = D(logistic ? 0.5 * e : e);
+            }
+        } else {
+            D d = D(0);
+            for (int64_t f = 0; f < nf; ++f) d += to_arith<D>(m[f]) * to_arith<D>(x[f]);
+            if (Yhat != nullptr) Yhat[i] = from_arith<T>(d);
+            if (E != nullptr) E[i] = d - (Y != nullptr ? to_arith<D>(Y[i]) : D(0));
         }
     }
 }

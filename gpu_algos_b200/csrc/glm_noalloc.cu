@@ -26,7 +26,13 @@
 //    with events.
 //  - The first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture begins.
+//    first call before any stream capture begins.  The cached address lives
+//    as long as the process: after cudaDeviceReset on a device, this entry
+//    point must not be called again in that process (the module would be
+//    reloaded and the array could move).
+//  - When the array, not the GPU, limits the CTAs a task gets (fewer than the
+//    planner's 148 SMs x CTAs per SM), each CTA walks more rows and the call
+//    slows in proportion.
 #include <mutex>
 
 #include "glm_common.cuh"

@@ -172,6 +172,28 @@ class PeerBackend(CudaBackend):
         self._sharded(X, M, Y, out, None, lam, alpha, True)
         return out
 
+    def fit(self, X, Y, lambda1, lambda2, n_power, n_iter, seed, beta=None, lipschitz=None):
+        """The whole sharded fit in one library call (glmb_fit_elastic_net_sharded_*):
+        the power iterations and ISTA steps, each partial summed over the group."""
+        from . import capi, glm
+
+        sfx = glm.SUFFIX[X.dtype]
+        nobs, ntasks, nf = X.shape
+        nt = Y.shape[2]
+        if beta is None:
+            beta = torch.empty((ntasks, nt, nf), dtype=X.dtype, device=X.device)
+        if lipschitz is None:
+            lipschitz = torch.empty((ntasks,), dtype=torch.float64, device=X.device)
+        need = int(getattr(capi.lib(), f"glmb_fit_workspace_size_{sfx}")(nf, nt, ntasks, nobs))
+        ws = self.workspace
+        if ws is None or ws.numel() * ws.element_size() < need:
+            ws = torch.empty(max(need, 1), dtype=torch.uint8, device=X.device)
+        capi.call(f"glmb_fit_elastic_net_sharded_{sfx}", X.data_ptr(), Y.data_ptr(), beta.data_ptr(),
+                  lipschitz.data_ptr(), nf, nt, ntasks, nobs, float(lambda1), float(lambda2), int(n_power),
+                  int(n_iter), int(seed) & (2**64 - 1), self.peer.ptr, ws.data_ptr(),
+                  ws.numel() * ws.element_size(), torch.cuda.current_stream().cuda_stream)
+        return beta, lipschitz
+
 
 def _all_reduce(t, group):
     if group is not None or (dist.is_available() and dist.is_initialized()):
@@ -212,6 +234,9 @@ class ShardedGLM:
         iteration on every rank; ``resume=(it, beta, lipschitz)`` restarts
         from a snapshot taken that way (skipping the power iteration).
         """
+        if checkpoint is None and resume is None and hasattr(self.backend, "fit"):
+            # the library runs the whole loop (PeerBackend)
+            return self.backend.fit(self.X_local, self.Y_local, lambda1, lambda2, n_power, n_iter, seed)
         ntasks, nf = self.X_local.shape[1], self.X_local.shape[2]
         nt = self.Y_local.shape[2]
         dev, dt = self.X_local.device, self.X_local.dtype

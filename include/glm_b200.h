@@ -199,7 +199,13 @@ int glmb_gradient_loss_f64(const double* X, const double* M, const double* Y, do
  * (else GLMB_ERR_UNSUPPORTED).  All calls on a device share the array:
  * calls whose kernels overlap on the GPU race, so order them (one stream or
  * events).  The first call on each device looks up the array's address;
- * make it before any stream capture begins.
+ * make it before any stream capture begins.  That address is kept for the
+ * life of the process: after cudaDeviceReset on a device, do not call this
+ * entry point again in that process.  Throughput: the array holds one double
+ * per (task, target, feature) per CTA, so a task gets at most
+ * 524288 / (nfeatures*ntargets*ntasks) CTAs; once that falls below the CTAs
+ * the single-pass kernel would otherwise use (148 SMs x CTAs per SM, shared
+ * by the tasks) the call runs on fewer, longer CTAs and slows accordingly.
  * ---------------------------------------------------------------------- */
 int glmb_gradient_noalloc_f32(const float* X, const float* M, const float* Y, float* grad_M,
                               float* Yhat, int64_t nfeatures, int64_t ntargets, int64_t ntasks,

@@ -5,7 +5,7 @@ command line), the input of ``tests/test_harness_replay.py``.
 
 Usage (on a host with a B200 and the built executables)::
 
-    python tests/golden/harness_run.py [--jobs 8]
+    python tests/golden/harness_run.py [--jobs 8] [--out PATH]
 """
 from __future__ import annotations
 
@@ -38,16 +38,17 @@ def run_one(cmd, timeout=300):
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--jobs", type=int, default=8)
+    p.add_argument("--out", default=OUT)
     a = p.parse_args()
     with open(COMMANDS) as f:
         commands = json.load(f)["commands"]
     with cf.ThreadPoolExecutor(max_workers=a.jobs) as ex:
         results = list(ex.map(run_one, commands))
     results.sort(key=lambda r: " ".join(r["cmd"]))
-    with gzip.open(OUT, "wt") as f:
+    with gzip.open(a.out, "wt") as f:
         json.dump({"outputs": results}, f)
     bad = [r for r in results if r["return_code"] != 0 or "[SUCCESS]" not in r["stdout"]]
-    print(f"{len(results)} runs, {len(bad)} without [SUCCESS] -> {OUT}")
+    print(f"{len(results)} runs, {len(bad)} without [SUCCESS] -> {a.out}")
     for r in bad[:10]:
         print(" ".join(r["cmd"]), r["return_code"], r["stdout"][-300:], r["stderr"][-300:])
     return 1 if bad else 0
