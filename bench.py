@@ -18,6 +18,7 @@ Other workloads (--workload):
              float64 (tasks sharded across ranks, no collective)
   gradient_f16  the default workload with float16 X, y and model (float
              arithmetic in the kernel; half the HBM bytes per row)
+  gradient_bf16 the same with bfloat16
   dense      wide dense gradient on the tensor cores (3xTF32): nobs 2^20,
              nfeatures 4096, ntargets 256, float32, X ~ U(-1,1)/sqrt(4096),
              lambda2 0.001 (observations sharded)
@@ -62,7 +63,7 @@ class Workload:
     nf: int
     nt: int
     ntasks: int
-    dtype: str  # "f16" | "f32" | "f64"
+    dtype: str  # "f16" | "bf16" | "f32" | "f64"
     x: str  # "uniform" (U(-1,1)) | "normal" (N(0,1)), times x_scale
     noise: float
     shard: str  # "obs" | "tasks" | "replica"
@@ -86,6 +87,7 @@ WORKLOADS = {
     "multitask": Workload("multitask", 1 << 18, 256, 16, 64, "f64", "normal", 0.05, "tasks", lam=0.1,
                           independent_beta=True, block=1 << 14),
     "gradient_f16": Workload("gradient_f16", 1 << 24, 128, 1, 1, "f16", "uniform", 0.1, "obs", lam=0.01),
+    "gradient_bf16": Workload("gradient_bf16", 1 << 24, 128, 1, 1, "bf16", "uniform", 0.1, "obs", lam=0.01),
     "dense": Workload("dense", 1 << 20, 4096, 256, 1, "f32", "uniform", 0.01, "obs", lam=0.001,
                       x_scale=4096 ** -0.5, block=1 << 15),
     "fit": Workload("fit", 1 << 26, 512, 1, 1, "f32", "normal", 0.1, "obs", kind="fit", sparsity=0.1,
@@ -114,8 +116,8 @@ def parse_args():
     if a.nobs is not None:
         w = Workload(**{**w.__dict__, "nobs": a.nobs, "block": min(w.block, a.nobs)})
     a.w = w
-    default_steps = {"gradient": 500, "gradient_f16": 500, "driver": 2000, "multitask": 20, "dense": 20,
-                     "fit": 2}[w.name]
+    default_steps = {"gradient": 500, "gradient_f16": 500, "gradient_bf16": 500, "driver": 2000, "multitask": 20,
+                     "dense": 20, "fit": 2}[w.name]
     a.steps = a.steps if a.steps is not None else default_steps
     a.warmup = a.warmup if a.warmup is not None else (1 if w.kind == "fit" else 10)
     return a
@@ -205,25 +207,33 @@ def host_threads() -> int:
 # CPU: the reference's algorithm (oracle port) on the host cores
 # --------------------------------------------------------------------------
 def cpu_problem(w: Workload, rows: int):
+    """Host copy of a `rows`-observation sample (bfloat16 as uint16 bit patterns)."""
     import numpy as np
 
     rng = np.random.default_rng(7)
-    dt = {"f16": np.float16, "f32": np.float32, "f64": np.float64}[w.dtype]
+    if w.dtype == "bf16":
+        from oracle import pyoracle
+
+        dt, conv, back = np.float32, pyoracle.bf16_bits, pyoracle.bf16_to_f32
+    else:
+        dt = {"f16": np.float16, "f32": np.float32, "f64": np.float64}[w.dtype]
+        conv = back = (lambda a: a)  # noqa: E731
     if w.x == "uniform":
         X = rng.uniform(-1, 1, (rows, w.ntasks, w.nf)).astype(dt)
     else:
         X = rng.normal(size=(rows, w.ntasks, w.nf)).astype(dt)
-    X *= dt(w.x_scale)
-    b = rng.normal(size=(w.ntasks, w.nt, w.nf)).astype(dt)
-    Y = (np.einsum("otf,tkf->otk", X.astype(np.float64), b.astype(np.float64))
-         + w.noise * rng.normal(size=(rows, w.ntasks, w.nt))).astype(dt)
+    X = conv(X * dt(w.x_scale))
+    b = conv(rng.normal(size=(w.ntasks, w.nt, w.nf)).astype(dt))
+    Y = conv((np.einsum("otf,tkf->otk", back(X).astype(np.float64), back(b).astype(np.float64))
+              + w.noise * rng.normal(size=(rows, w.ntasks, w.nt))).astype(dt))
     return X, b, Y
 
 
 def cpu_pass(pyoracle, w: Workload, X, b, Y):
+    bf16 = w.dtype == "bf16"
     if w.kind == "fit":
-        return pyoracle.gradient(X, b, Y, w.lambda2, 0.0, True)
-    return pyoracle.gradient(X, b, Y, w.lam, w.alpha, True)
+        return pyoracle.gradient(X, b, Y, w.lambda2, 0.0, True, bf16=bf16)
+    return pyoracle.gradient(X, b, Y, w.lam, w.alpha, True, bf16=bf16)
 
 
 def cpu_sample_rate(w: Workload, rows: int, reps: int = 3):
@@ -243,8 +253,8 @@ def cpu_sample_rate(w: Workload, rows: int, reps: int = 3):
 
 
 def cpu_rows(w: Workload) -> int:
-    return min(w.nobs, {"gradient": 1 << 21, "gradient_f16": 1 << 20, "driver": 8192, "multitask": 4096,
-                        "dense": 4096, "fit": 1 << 19}[w.name])
+    return min(w.nobs, {"gradient": 1 << 21, "gradient_f16": 1 << 20, "gradient_bf16": 1 << 20, "driver": 8192,
+                        "multitask": 4096, "dense": 4096, "fit": 1 << 19}[w.name])
 
 
 def run_reference(args):
@@ -365,7 +375,7 @@ def make_local(w: Workload, rank: int, world: int, seed: int, device):
 
     from gpu_algos_b200.sharded import obs_range, task_range
 
-    dt = {"f16": torch.float16, "f32": torch.float32, "f64": torch.float64}[w.dtype]
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32, "f64": torch.float64}[w.dtype]
     if w.shard == "obs":
         assert w.nobs % (world * w.block) == 0, "nobs must split into whole generation blocks per rank"
         lo, hi = obs_range(w.nobs, world, rank)
@@ -699,6 +709,7 @@ def run_ours(args):
                      else "fallback 6650 GB/s")
         kernel_name = {"gradient": "glm_rows_kernel (+ finalize): one glmb_gradient call",
                        "gradient_f16": "glm_rows_kernel<__half> (+ finalize): one glmb_gradient_f16 call",
+                       "gradient_bf16": "glm_rows_kernel<__nv_bfloat16> (+ finalize): one glmb_gradient_bf16 call",
                        "driver": "glm_rows_kernel (+ finalize): one glmb_gradient call",
                        "multitask": "glm_tiles_f64_kernel (+ finalize): one glmb_gradient_f64 call",
                        "dense": "glm_dense_gemm_kernel x2 on CTA pairs (GEMM1 residuals, GEMM2 split-K X^T R) "

@@ -33,7 +33,9 @@ GRAD_Y_ZERO = 0x4
 GRAD_LOGISTIC = 0x8
 
 #: the eleven element types of the reference mains, by C-ABI suffix
-SUFFIXES = ("f16", "f32", "f64", "i8", "i16", "i32", "i64", "u8", "u16", "u32", "u64")
+REFERENCE_SUFFIXES = ("f16", "f32", "f64", "i8", "i16", "i32", "i64", "u8", "u16", "u32", "u64")
+#: every element type of predict / gradient / loss: the reference's eleven and bfloat16
+SUFFIXES = REFERENCE_SUFFIXES + ("bf16",)
 FLOATING = ("f32", "f64")
 
 

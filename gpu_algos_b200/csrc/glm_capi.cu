@@ -81,9 +81,10 @@ int check_device() {
 
 template <typename T>
 constexpr bool kRowsType = std::is_same_v<T, float> || std::is_same_v<T, double>;
-// element types the fused rows kernel is built for (half: float arithmetic on packed 8- or 16-byte loads)
+// element types the fused rows kernel is built for (half, bfloat16: float arithmetic on packed 4- to
+// 16-byte loads)
 template <typename T>
-constexpr bool kRowsKernelType = kRowsType<T> || std::is_same_v<T, __half>;
+constexpr bool kRowsKernelType = kRowsType<T> || kHalf16<T>;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -184,7 +185,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
     if (flags & ~(GLMB_GRAD_REGULARIZE | GLMB_GRAD_WRITE_YHAT | GLMB_GRAD_Y_ZERO | GLMB_GRAD_LOGISTIC))
         return GLMB_ERR_INVALID_VALUE;
     const bool logistic = (flags & GLMB_GRAD_LOGISTIC) != 0;
-    if (logistic && !std::is_floating_point_v<T> && !std::is_same_v<T, __half>) return GLMB_ERR_INVALID_VALUE;
+    if (logistic && !std::is_floating_point_v<T> && !kHalf16<T>) return GLMB_ERR_INVALID_VALUE;
     const bool reg = (flags & GLMB_GRAD_REGULARIZE) != 0;
     const bool write_yhat = (flags & GLMB_GRAD_WRITE_YHAT) != 0;
     const bool y_zero = (flags & GLMB_GRAD_Y_ZERO) != 0;
@@ -453,6 +454,7 @@ const char* glmb_last_path(void) { return glmb::g_last_path; }
     }
 
 GLMB_DEFINE_BASIC(f16, uint16_t, __half)
+GLMB_DEFINE_BASIC(bf16, uint16_t, __nv_bfloat16)
 GLMB_DEFINE_BASIC(f32, float, float)
 GLMB_DEFINE_BASIC(f64, double, double)
 GLMB_DEFINE_BASIC(i8, int8_t, int8_t)

@@ -3,6 +3,7 @@
 
 #include <utility>
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -53,6 +54,23 @@ struct Arith<__half> {
     using Acc = float;
     using Dot = float;
 };
+template <>
+struct Arith<__nv_bfloat16> {
+    using Acc = float;
+    using Dot = float;
+};
+
+// The 16-bit floating types: binary16 (__half) and bfloat16.  Both compute
+// in float and round to their own format on store.
+template <typename T>
+inline constexpr bool kHalf16 = std::is_same_v<T, __half> || std::is_same_v<T, __nv_bfloat16>;
+__device__ __forceinline__ float half16_to_float(__half v) { return __half2float(v); }
+__device__ __forceinline__ float half16_to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T float_to_half16(float f) {
+    if constexpr (std::is_same_v<T, __half>) return __float2half_rn(f);
+    else return __float2bfloat16_rn(f);
+}
 #define GLMB_INT_ARITH(T, U)   \
     template <>                \
     struct Arith<T> {          \
@@ -71,8 +89,8 @@ GLMB_INT_ARITH(uint64_t, uint64_t)
 
 template <typename A, typename T>
 __device__ __forceinline__ A to_arith(T v) {
-    if constexpr (std::is_same_v<T, __half>) {
-        return static_cast<A>(__half2float(v));
+    if constexpr (kHalf16<T>) {
+        return static_cast<A>(half16_to_float(v));
     } else {
         return static_cast<A>(v);
     }
@@ -80,8 +98,8 @@ __device__ __forceinline__ A to_arith(T v) {
 
 template <typename T, typename A>
 __device__ __forceinline__ T from_arith(A v) {
-    if constexpr (std::is_same_v<T, __half>) {
-        return __float2half_rn(static_cast<float>(v));
+    if constexpr (kHalf16<T>) {
+        return float_to_half16<T>(static_cast<float>(v));
     } else {
         return static_cast<T>(v);
     }
@@ -92,6 +110,8 @@ template <typename T>
 __host__ __device__ __forceinline__ T from_double(double d) {
     if constexpr (std::is_same_v<T, __half>) {
         return __double2half(d);
+    } else if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        return __double2bfloat16(d);
     } else {
         return static_cast<T>(d);
     }
@@ -101,8 +121,8 @@ template <typename T>
 __device__ __forceinline__ int sign_of(T v) {
     // include/cuda/cuda_utils.cuh:475-485 of the reference: is_positive /
     // is_negative; unsigned values are never negative, sign(0) = 0.
-    if constexpr (std::is_same_v<T, __half>) {
-        const float f = __half2float(v);
+    if constexpr (kHalf16<T>) {
+        const float f = half16_to_float(v);
         return f > 0.f ? 1 : (f < 0.f ? -1 : 0);
     } else if constexpr (std::is_unsigned_v<T>) {
         return v > T(0) ? 1 : 0;
@@ -113,12 +133,12 @@ __device__ __forceinline__ int sign_of(T v) {
 
 template <typename T>
 __device__ __forceinline__ bool t_gt0(T v) {
-    if constexpr (std::is_same_v<T, __half>) return __half2float(v) > 0.f;
+    if constexpr (kHalf16<T>) return half16_to_float(v) > 0.f;
     else return v > T(0);
 }
 template <typename T>
 __device__ __forceinline__ bool t_lt1(T v) {
-    if constexpr (std::is_same_v<T, __half>) return __half2float(v) < 1.f;
+    if constexpr (kHalf16<T>) return half16_to_float(v) < 1.f;
     else return v < T(1);
 }
 
@@ -220,47 +240,58 @@ struct VecLoad<double, 2> {
                      : "l"(p));
     }
 };
-template <>
-struct VecLoad<__half, 8> {
-    __device__ __forceinline__ static void load(const __half* p, __half (&v)[8]) {
+// 16-bit floats (__half, bfloat16): raw 16-bit patterns, element 2i in the
+// low half of 32-bit word i.
+template <typename T>
+__device__ __forceinline__ T half16_from_bits(unsigned short b) {
+    if constexpr (std::is_same_v<T, __half>) return __ushort_as_half(b);
+    else return __ushort_as_bfloat16(b);
+}
+template <typename T>
+    requires kHalf16<T>
+struct VecLoad<T, 8> {
+    __device__ __forceinline__ static void load(const T* p, T (&v)[8]) {
         uint32_t r[4];
         asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                      : "l"(p));
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {  // element 2i is the low half of word i
-            v[2 * i] = __ushort_as_half(static_cast<unsigned short>(r[i] & 0xffffu));
-            v[2 * i + 1] = __ushort_as_half(static_cast<unsigned short>(r[i] >> 16));
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = half16_from_bits<T>(static_cast<unsigned short>(r[i] & 0xffffu));
+            v[2 * i + 1] = half16_from_bits<T>(static_cast<unsigned short>(r[i] >> 16));
         }
     }
 };
-template <>
-struct VecLoad<__half, 4> {
-    __device__ __forceinline__ static void load(const __half* p, __half (&v)[4]) {
+template <typename T>
+    requires kHalf16<T>
+struct VecLoad<T, 4> {
+    __device__ __forceinline__ static void load(const T* p, T (&v)[4]) {
         uint32_t r[2];
         asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "l"(p));
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-            v[2 * i] = __ushort_as_half(static_cast<unsigned short>(r[i] & 0xffffu));
-            v[2 * i + 1] = __ushort_as_half(static_cast<unsigned short>(r[i] >> 16));
+            v[2 * i] = half16_from_bits<T>(static_cast<unsigned short>(r[i] & 0xffffu));
+            v[2 * i + 1] = half16_from_bits<T>(static_cast<unsigned short>(r[i] >> 16));
         }
     }
 };
-template <>
-struct VecLoad<__half, 2> {
-    __device__ __forceinline__ static void load(const __half* p, __half (&v)[2]) {
+template <typename T>
+    requires kHalf16<T>
+struct VecLoad<T, 2> {
+    __device__ __forceinline__ static void load(const T* p, T (&v)[2]) {
         uint32_t r;
         asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
-        v[0] = __ushort_as_half(static_cast<unsigned short>(r & 0xffffu));
-        v[1] = __ushort_as_half(static_cast<unsigned short>(r >> 16));
+        v[0] = half16_from_bits<T>(static_cast<unsigned short>(r & 0xffffu));
+        v[1] = half16_from_bits<T>(static_cast<unsigned short>(r >> 16));
     }
 };
-template <>
-struct VecLoad<__half, 1> {
-    __device__ __forceinline__ static void load(const __half* p, __half (&v)[1]) {
+template <typename T>
+    requires kHalf16<T>
+struct VecLoad<T, 1> {
+    __device__ __forceinline__ static void load(const T* p, T (&v)[1]) {
         unsigned short r;
         asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
-        v[0] = __ushort_as_half(r);
+        v[0] = half16_from_bits<T>(r);
     }
 };
 template <>

@@ -240,6 +240,7 @@ int generic_gradient(const T* X, const T* M, const T* Y, T* grad, T* Yhat, doubl
                                      size_t, cudaStream_t, PartsFinisher, void*, bool);
 
 GLMB_INSTANTIATE_GENERIC(__half)
+GLMB_INSTANTIATE_GENERIC(__nv_bfloat16)
 GLMB_INSTANTIATE_GENERIC(float)
 GLMB_INSTANTIATE_GENERIC(double)
 GLMB_INSTANTIATE_GENERIC(int8_t)
@@ -253,6 +254,8 @@ GLMB_INSTANTIATE_GENERIC(uint64_t)
 
 template int finalize_launch<__half, double>(const double*, int64_t, int64_t, const __half*, __half*,
                                              double*, double, double, bool, cudaStream_t);
+template int finalize_launch<__nv_bfloat16, double>(const double*, int64_t, int64_t, const __nv_bfloat16*,
+                                                    __nv_bfloat16*, double*, double, double, bool, cudaStream_t);
 template int finalize_launch<float, double>(const double*, int64_t, int64_t, const float*, float*,
                                             double*, double, double, bool, cudaStream_t);
 template int finalize_launch<double, double>(const double*, int64_t, int64_t, const double*,

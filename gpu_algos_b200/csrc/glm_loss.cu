@@ -39,6 +39,10 @@ template <>
 struct LossAcc<__half> {
     using type = double;
 };
+template <>
+struct LossAcc<__nv_bfloat16> {
+    using type = double;
+};
 
 template <typename L, typename T>
 __device__ __forceinline__ L load_as(const T* p, int64_t i) {
@@ -176,6 +180,7 @@ template int loss_from_partials_launch<double>(const double*, int64_t, const dou
     template int loss_launch<T>(const T*, const T*, const T*, T*, int64_t, int64_t, int64_t, int64_t, double, \
                                 double, void*, size_t, cudaStream_t);
 GLMB_INSTANTIATE_LOSS(__half)
+GLMB_INSTANTIATE_LOSS(__nv_bfloat16)
 GLMB_INSTANTIATE_LOSS(float)
 GLMB_INSTANTIATE_LOSS(double)
 GLMB_INSTANTIATE_LOSS(int8_t)

@@ -1,6 +1,6 @@
-// glm_rows.cuh -- fused row-streaming GLM kernel for float / double / half
-// (half: float arithmetic on packed loads of 4 or 8 values, half the HBM bytes
-// of float per feature).
+// glm_rows.cuh -- fused row-streaming GLM kernel for float / double / half /
+// bfloat16 (16-bit types: float arithmetic on packed loads of 2-8 values,
+// half the HBM bytes of float per feature).
 //
 // One pass over X computes, for every row x = X[obs, task, :],
 //     yhat_t = sum_f M[task, t, f] * x_f          (t < ntargets)
@@ -84,30 +84,97 @@ struct RowsShape {
     static constexpr size_t SMEM = size_t(kRowsWarps) * SLOTS * sizeof(double);
 };
 
-// Register image of one lane's VEC consecutive elements of a row: the
-// elements themselves, or -- for half with VEC >= 2 -- pairs packed in 32-bit
-// words (element 2i in the low half of word i), converted at use, so a batch
-// of half rows takes half the registers of a batch of float rows.
+// Register image of one lane's VEC consecutive elements of a row and of the
+// matching model coefficients, with the two operations the kernel applies to
+// them: the dot-product step d += m . x (elements in order) and the gradient
+// step acc += r * x.  Generic types hold the elements themselves, in the
+// arithmetic type D.
 template <typename T, int VEC>
 struct XRegs {
     static constexpr int N = VEC;
     using W = T;
+    template <typename D>
+    using MW = D;
+    template <typename D>
+    static constexpr int MN = VEC;
     __device__ __forceinline__ static void load(const T* p, W (&w)[N]) { VecLoad<T, VEC>::load(p, w); }
     template <typename D>
-    __device__ __forceinline__ static D get(const W (&w)[N], int v) {
-        return D(w[v]);
+    __device__ __forceinline__ static void load_m(const T* mrow, int64_t f0, int64_t nf, bool ok, D (&m)[VEC]) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) m[v] = (ok && f0 + v < nf) ? to_arith<D>(mrow[f0 + v]) : D(0);
     }
     template <typename D>
-    __device__ __forceinline__ static D get_again(const W (&w)[N], int v) {
-        return D(w[v]);
+    __device__ __forceinline__ static D dot(const D (&m)[VEC], const W (&w)[N], D d) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) d = fma(m[v], D(w[v]), d);
+        return d;
+    }
+    template <typename D>
+    __device__ __forceinline__ static void axpy(D r, const W (&w)[N], D (&acc)[VEC]) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[v] = fma(r, D(w[v]), acc[v]);
     }
 };
-template <int VEC>
-struct XRegs<__half, VEC> {
-    static_assert(VEC == 2 || VEC == 4 || VEC == 8, "packed half vectors");
+
+// 16-bit float rows (__half, bfloat16), VEC >= 2: elements and coefficients
+// stay packed in pairs in 32-bit words (element 2i in the low half of word
+// i), so a batch of such rows takes half the registers of a batch of float
+// rows.  The dot step is the mixed-precision fma.rn.f32.{f16,bf16}
+// (16-bit x 16-bit + f32, rounded once): the product of two 16-bit floats is
+// exact in float, so it equals converting both operands and a float FMA,
+// with no conversion instruction.  The gradient step converts each pair and
+// updates two float accumulators with one packed fma.rn.f32x2 (per element
+// the same rounding as a scalar FMA).  A 16-bit row carries the float row's
+// arithmetic on half the bytes, so these instruction counts (one per
+// element for the dot, one and a half for the gradient, against two and two)
+// decide whether it keeps up with HBM.
+template <typename T>
+__device__ __forceinline__ float fma_half16_pair(uint32_t m, uint32_t x, float d) {
+    if constexpr (std::is_same_v<T, __half>) {
+        asm("{\n\t.reg .f16 ml, mh, xl, xh;\n\t"
+            "mov.b32 {ml, mh}, %1;\n\tmov.b32 {xl, xh}, %2;\n\t"
+            "fma.rn.f32.f16 %0, ml, xl, %0;\n\tfma.rn.f32.f16 %0, mh, xh, %0;\n\t}"
+            : "+f"(d)
+            : "r"(m), "r"(x));
+    } else {
+        asm("{\n\t.reg .b16 ml, mh, xl, xh;\n\t"
+            "mov.b32 {ml, mh}, %1;\n\tmov.b32 {xl, xh}, %2;\n\t"
+            "fma.rn.f32.bf16 %0, ml, xl, %0;\n\tfma.rn.f32.bf16 %0, mh, xh, %0;\n\t}"
+            : "+f"(d)
+            : "r"(m), "r"(x));
+    }
+    return d;
+}
+template <typename T>
+__device__ __forceinline__ void axpy_half16_pair(float r, uint32_t x, float& a0, float& a1) {
+    if constexpr (std::is_same_v<T, __half>) {
+        asm("{\n\t.reg .f16 xl, xh;\n\t.reg .f32 x0, x1;\n\t.reg .b64 a, xx, rr;\n\t"
+            "mov.b32 {xl, xh}, %3;\n\tcvt.f32.f16 x0, xl;\n\tcvt.f32.f16 x1, xh;\n\t"
+            "mov.b64 a, {%0, %1};\n\tmov.b64 xx, {x0, x1};\n\tmov.b64 rr, {%2, %2};\n\t"
+            "fma.rn.f32x2 a, rr, xx, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "f"(r), "r"(x));
+    } else {
+        // bfloat16 -> float is exact: the 16 bits become the high half of the float
+        asm("{\n\t.reg .b32 x0, x1;\n\t.reg .b64 a, xx, rr;\n\t"
+            "shl.b32 x0, %3, 16;\n\tand.b32 x1, %3, 0xffff0000;\n\t"
+            "mov.b64 a, {%0, %1};\n\tmov.b64 xx, {x0, x1};\n\tmov.b64 rr, {%2, %2};\n\t"
+            "fma.rn.f32x2 a, rr, xx, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "f"(r), "r"(x));
+    }
+}
+template <typename T, int VEC>
+    requires kHalf16<T>
+struct XRegs<T, VEC> {
+    static_assert(VEC == 2 || VEC == 4 || VEC == 8, "packed 16-bit vectors");
     static constexpr int N = VEC / 2;
     using W = uint32_t;
-    __device__ __forceinline__ static void load(const __half* p, W (&w)[N]) {
+    template <typename D>
+    using MW = uint32_t;
+    template <typename D>
+    static constexpr int MN = N;
+    __device__ __forceinline__ static void load(const T* p, W (&w)[N]) {
         if constexpr (N == 4) {
             asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
                          : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
@@ -119,37 +186,48 @@ struct XRegs<__half, VEC> {
         }
     }
     template <typename D>
-    __device__ __forceinline__ static D get(const W (&w)[N], int v) {
-        const uint32_t x = w[v >> 1];
-        return D(__half2float(__ushort_as_half(static_cast<unsigned short>((v & 1) ? (x >> 16) : (x & 0xffffu)))));
+    __device__ __forceinline__ static void load_m(const T* mrow, int64_t f0, int64_t nf, bool ok, uint32_t (&m)[N]) {
+        const unsigned short* bits = reinterpret_cast<const unsigned short*>(mrow);
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const unsigned short lo = (ok && f0 + 2 * i < nf) ? bits[f0 + 2 * i] : 0;
+            const unsigned short hi = (ok && f0 + 2 * i + 1 < nf) ? bits[f0 + 2 * i + 1] : 0;
+            m[i] = uint32_t(lo) | (uint32_t(hi) << 16);
+        }
     }
-    // The same value, converted again where the gradient loop uses it.  Left
-    // to itself the compiler keeps the dot loop's converted floats (a batch
-    // of 8 rows: 32 registers) alive across the butterfly; a conversion it
-    // cannot match with those keeps only the packed pairs alive, which takes
-    // the kernel from 104 to 80 registers and from 2 to 3 CTAs per SM.
     template <typename D>
-    __device__ __forceinline__ static D get_again(const W (&w)[N], int v) {
-        float f;
-        if (v & 1)
-            asm("{ .reg .f16 lo, hi; mov.b32 {lo, hi}, %1; cvt.f32.f16 %0, hi; }" : "=f"(f) : "r"(w[v >> 1]));
-        else
-            asm("{ .reg .f16 lo, hi; mov.b32 {lo, hi}, %1; cvt.f32.f16 %0, lo; }" : "=f"(f) : "r"(w[v >> 1]));
-        return D(f);
+    __device__ __forceinline__ static D dot(const uint32_t (&m)[N], const W (&w)[N], D d) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) d = fma_half16_pair<T>(m[i], w[i], d);
+        return d;
+    }
+    template <typename D>
+    __device__ __forceinline__ static void axpy(D r, const W (&w)[N], D (&acc)[VEC]) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) axpy_half16_pair<T>(r, w[i], acc[2 * i], acc[2 * i + 1]);
     }
 };
-template <>
-struct XRegs<__half, 1> {
+template <typename T>
+    requires kHalf16<T>
+struct XRegs<T, 1> {
     static constexpr int N = 1;
-    using W = __half;
-    __device__ __forceinline__ static void load(const __half* p, W (&w)[1]) { VecLoad<__half, 1>::load(p, w); }
+    using W = T;
     template <typename D>
-    __device__ __forceinline__ static D get(const W (&w)[1], int) {
-        return D(__half2float(w[0]));
+    using MW = D;
+    template <typename D>
+    static constexpr int MN = 1;
+    __device__ __forceinline__ static void load(const T* p, W (&w)[1]) { VecLoad<T, 1>::load(p, w); }
+    template <typename D>
+    __device__ __forceinline__ static void load_m(const T* mrow, int64_t f0, int64_t nf, bool ok, D (&m)[1]) {
+        m[0] = (ok && f0 < nf) ? to_arith<D>(mrow[f0]) : D(0);
     }
     template <typename D>
-    __device__ __forceinline__ static D get_again(const W (&w)[1], int) {
-        return D(__half2float(w[0]));
+    __device__ __forceinline__ static D dot(const D (&m)[1], const W (&w)[1], D d) {
+        return fma(m[0], D(half16_to_float(w[0])), d);
+    }
+    template <typename D>
+    __device__ __forceinline__ static void axpy(D r, const W (&w)[1], D (&acc)[1]) {
+        acc[0] = fma(r, D(half16_to_float(w[0])), acc[0]);
     }
 };
 
@@ -204,16 +282,15 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
     const int u_mine = FULL ? (lane >> (5 - LOG2U)) : 0;
 
     // Model coefficients of this task, in registers.
-    D m[NT][CPL][VEC];
+    using MW = typename XR::template MW<D>;
+    constexpr int MN = XR::template MN<D>;
+    MW m[NT][CPL][MN];
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int c = 0; c < CPL; ++c)
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) {
-                const int64_t f = int64_t(c * S + ls) * VEC + v;
-                m[t][c][v] = (t < nt && f < nf) ? to_arith<D>(M[(task * nt + t) * nf + f]) : D(0);
-            }
+            XR::template load_m<D>(M + (task * nt + (t < nt ? t : 0)) * nf, int64_t(c * S + ls) * VEC, nf, t < nt,
+                                   m[t][c]);
 
     D acc[NT][CPL][VEC];
     double sq = 0.0;  // LOSS: this lane's share of sum r^2
@@ -295,9 +372,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                 for (int u = 0; u < U; ++u) {
                     D d = D(0);
 #pragma unroll
-                    for (int c = 0; c < CPL; ++c)
-#pragma unroll
-                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], XR::template get<D>(xb[u][c], v), d);
+                    for (int c = 0; c < CPL; ++c) d = XR::template dot<D>(m[t][c], xb[u][c], d);
                     vals[u] = d;
                 }
                 // transposed butterfly over the first log2(U) lane bits
@@ -333,9 +408,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                     for (int u = 0; u < U; ++u) {
                         const D r = __shfl_sync(0xffffffffu, r_mine, u << (5 - LOG2U));
 #pragma unroll
-                        for (int c = 0; c < CPL; ++c)
-#pragma unroll
-                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get_again<D>(xb[u][c], v), acc[t][c][v]);
+                        for (int c = 0; c < CPL; ++c) XR::template axpy<D>(r, xb[u][c], acc[t][c]);
                     }
                 }
             }
@@ -347,9 +420,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                 for (int t = 0; t < NT; ++t) {
                     D d = D(0);
 #pragma unroll
-                    for (int c = 0; c < CPL; ++c)
-#pragma unroll
-                        for (int v = 0; v < VEC; ++v) d = fma(m[t][c][v], XR::template get<D>(xb[u][c], v), d);
+                    for (int c = 0; c < CPL; ++c) d = XR::template dot<D>(m[t][c], xb[u][c], d);
                     for (int off = S >> 1; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
                     if constexpr (LOGIT) d = sigmoid(d);
                     if constexpr (WRITE) {
@@ -361,9 +432,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                             if (ls == 0 && t < nt && obs < obs_end) sq = fma(double(r), double(r), sq);
                         }
 #pragma unroll
-                        for (int c = 0; c < CPL; ++c)
-#pragma unroll
-                            for (int v = 0; v < VEC; ++v) acc[t][c][v] = fma(r, XR::template get_again<D>(xb[u][c], v), acc[t][c][v]);
+                        for (int c = 0; c < CPL; ++c) XR::template axpy<D>(r, xb[u][c], acc[t][c]);
                     }
                 }
             }

@@ -19,6 +19,7 @@ from . import capi
 
 SUFFIX = {
     torch.float16: "f16",
+    torch.bfloat16: "bf16",
     torch.float32: "f32",
     torch.float64: "f64",
     torch.int8: "i8",

@@ -31,7 +31,10 @@
  *   - Types: f16 (__half bits), f32, f64, i8, i16, i32, i64, u8, u16, u32,
  *     u64 -- the eleven `--type` values of the reference mains
  *     (src/cuda/benchmarks/glm/glm_gradient_xyyhat.cu:38-62).  Integer types
- *     compute modulo 2^bits, as the reference's integer kernels do.
+ *     compute modulo 2^bits, as the reference's integer kernels do.  Also
+ *     bf16 (bfloat16 bits), beyond the reference's type set: float
+ *     arithmetic and rounding to bfloat16 on store, as f16 does with
+ *     binary16.
  */
 #ifndef GLM_B200_H
 #define GLM_B200_H
@@ -114,6 +117,7 @@ const char* glmb_last_path(void);
                             glmb_stream_t stream);
 
 GLMB_DECLARE_PREDICT(f16, uint16_t)
+GLMB_DECLARE_PREDICT(bf16, uint16_t)
 GLMB_DECLARE_PREDICT(f32, float)
 GLMB_DECLARE_PREDICT(f64, double)
 GLMB_DECLARE_PREDICT(i8, int8_t)
@@ -126,6 +130,7 @@ GLMB_DECLARE_PREDICT(u32, uint32_t)
 GLMB_DECLARE_PREDICT(u64, uint64_t)
 
 GLMB_DECLARE_GRADIENT(f16, uint16_t)
+GLMB_DECLARE_GRADIENT(bf16, uint16_t)
 GLMB_DECLARE_GRADIENT(f32, float)
 GLMB_DECLARE_GRADIENT(f64, double)
 GLMB_DECLARE_GRADIENT(i8, int8_t)
@@ -143,7 +148,7 @@ GLMB_DECLARE_GRADIENT(u64, uint64_t)
  * over every target, task and observation, lambda and alpha taken in T.
  * Replaces Glm_loss_myyhat_kernel<T>::run_device_kernel
  * (include/cuda/kernels/glm/glm_loss_myyhat.cuh:331-363; host definition
- * :365-401).  Y == NULL means zeros.  float/double/half sum in double,
+ * :365-401).  Y == NULL means zeros.  float/double/half/bfloat16 sum in double,
  * integer types modulo 2^bits (bit-exact with the reference).  Scratch:
  * the gradient workspace of the same shape is enough (or NULL: stream-
  * ordered allocation).  Two launches, one streaming pass over Y and Yhat.
@@ -155,6 +160,7 @@ GLMB_DECLARE_GRADIENT(u64, uint64_t)
                         size_t workspace_bytes, glmb_stream_t stream);
 
 GLMB_DECLARE_LOSS(f16, uint16_t)
+GLMB_DECLARE_LOSS(bf16, uint16_t)
 GLMB_DECLARE_LOSS(f32, float)
 GLMB_DECLARE_LOSS(f64, double)
 GLMB_DECLARE_LOSS(i8, int8_t)

@@ -9,6 +9,8 @@
  * reference's Eigen products run in the integer type itself, which wraps;
  * wrapping arithmetic is a ring homomorphism, so any summation order gives
  * the same bits), half computes in float and rounds to binary16 on store.
+ * bfloat16 (not a type of the reference) is treated like half: float
+ * arithmetic, rounded to bfloat16 on store.
  *
  * Summation order.  The reference's product 2*(M*X^T - Y^T)*X
  * (glm_gradient_xyyhat.cuh:839) is an Eigen GEMM, whose depth (obs) loop is
@@ -61,6 +63,45 @@ static inline uint16_t f2h(float f) {
     uint16_t h;
     memcpy(&h, &x, sizeof(h));
     return h;
+}
+/* the reference's Number(double) for half: one rounding from double */
+static inline uint16_t d2h(double d) {
+    _Float16 x = (_Float16)d;
+    uint16_t h;
+    memcpy(&h, &x, sizeof(h));
+    return h;
+}
+
+/* ---- bfloat16 helpers (bit operations, round-to-nearest-even) ----
+ * bfloat16 is the high half of a binary32: widening is a shift; narrowing
+ * adds 0x7fff plus the kept LSB (ties to even) and keeps the high half,
+ * NaNs stay quiet NaNs.  From double the value is first narrowed to float
+ * with round-to-odd (truncate, set the LSB when inexact), which makes the
+ * second rounding to 8 significant bits equal to one direct rounding. */
+static inline float b2f(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, sizeof(f));
+    return f;
+}
+static inline uint16_t f2b(float f) {
+    uint32_t u;
+    memcpy(&u, &f, sizeof(u));
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static inline uint16_t d2b(double d) {
+    if (d != d) return f2b((float)d);
+    float t = (float)d;
+    if ((double)t != d) {
+        if (fabs((double)t) > fabs(d)) t = nextafterf(t, 0.0f);
+        uint32_t u;
+        memcpy(&u, &t, sizeof(u));
+        u |= 1u;
+        memcpy(&t, &u, sizeof(t));
+    }
+    return f2b(t);
 }
 
 /* ---- per-type load (T -> A), store (A -> T), from-double and sign ---- */
@@ -227,13 +268,24 @@ ORACLE_DEFINE(f64, double, double, LD_D, ST_D, FROMD_D, GT0, LT0, LT1, SIGN_SIGN
 /* half: uint16_t bit patterns, float arithmetic */
 #define LD_H(v) h2f(v)
 #define ST_H(a) f2h((float)(a))
-#define FROMD_H(d) f2h((float)(d))
+#define FROMD_H(d) d2h(d)
 #define HGT0(v) (h2f(v) > 0.0f)
 #define HLT0(v) (h2f(v) < 0.0f)
 #define HLT1(v) (h2f(v) < 1.0f)
 #define HSIGN(v) ((h2f(v) > 0.0f) ? 1 : ((h2f(v) < 0.0f) ? -1 : 0))
 #define ABS_H(v) fabsf(h2f(v))
 ORACLE_DEFINE(f16, uint16_t, float, LD_H, ST_H, FROMD_H, HGT0, HLT0, HLT1, HSIGN, ABS_H);
+
+/* bfloat16: uint16_t bit patterns, float arithmetic */
+#define LD_B(v) b2f(v)
+#define ST_B(a) f2b((float)(a))
+#define FROMD_B(d) d2b(d)
+#define BGT0(v) (b2f(v) > 0.0f)
+#define BLT0(v) (b2f(v) < 0.0f)
+#define BLT1(v) (b2f(v) < 1.0f)
+#define BSIGN(v) ((b2f(v) > 0.0f) ? 1 : ((b2f(v) < 0.0f) ? -1 : 0))
+#define ABS_B(v) fabsf(b2f(v))
+ORACLE_DEFINE(bf16, uint16_t, float, LD_B, ST_B, FROMD_B, BGT0, BLT0, BLT1, BSIGN, ABS_B);
 
 /* integers: arithmetic modulo 2^32 (types up to 32 bits) or 2^64 */
 #define INT_FROMD(T) (T)

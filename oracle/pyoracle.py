@@ -10,6 +10,10 @@ expressed here as C-ordered NumPy arrays indexed ``[sheet, row, col]``:
 * ``X``     shape ``(nobs, ntasks, nfeatures)``
 * ``Y``     shape ``(nobs, ntasks, ntargets)``   (``Yhat`` alike)
 * ``M``     shape ``(ntasks, ntargets, nfeatures)``   (``grad`` alike)
+
+NumPy has no bfloat16 type: bfloat16 arrays travel as ``np.uint16`` bit
+patterns, and ``predict`` / ``gradient`` / ``loss`` take ``bf16=True`` to read
+them so (``bf16_bits`` and ``bf16_to_f32`` convert).
 """
 from __future__ import annotations
 
@@ -62,7 +66,7 @@ _INT = ctypes.c_int
 
 
 def _declare(L: ctypes.CDLL) -> None:
-    for sfx in SUFFIX.values():
+    for sfx in list(SUFFIX.values()) + ["bf16"]:
         getattr(L, f"oracle_glm_predict_{sfx}").argtypes = [_P, _P, _P, _I64, _I64, _I64, _I64]
         getattr(L, f"oracle_glm_gradient_{sfx}").argtypes = [
             _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _INT]
@@ -87,8 +91,24 @@ def _ptr(a: np.ndarray | None):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
-def _sfx(dtype) -> str:
+def _sfx(dtype, bf16: bool = False) -> str:
+    if bf16:
+        assert np.dtype(dtype) == np.uint16, "bfloat16 arrays are uint16 bit patterns"
+        return "bf16"
     return SUFFIX[np.dtype(dtype)]
+
+
+def bf16_bits(a) -> np.ndarray:
+    """float32 values -> bfloat16 bit patterns (round to nearest even; NaN stays NaN)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+
+
+def bf16_to_f32(b) -> np.ndarray:
+    """bfloat16 bit patterns -> float32 (exact)."""
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
 def set_threads(n: int) -> None:
@@ -106,18 +126,19 @@ def _dims(X, M):
     return nf, nt, ntasks, nobs
 
 
-def predict(X: np.ndarray, M: np.ndarray) -> np.ndarray:
+def predict(X: np.ndarray, M: np.ndarray, bf16: bool = False) -> np.ndarray:
     """Yhat[obs, task, t] = sum_f M[task, t, f] * X[obs, task, f]."""
     X = np.ascontiguousarray(X)
     M = np.ascontiguousarray(M, dtype=X.dtype)
     nf, nt, ntasks, nobs = _dims(X, M)
     Yhat = np.zeros((nobs, ntasks, nt), dtype=X.dtype)
-    getattr(lib(), f"oracle_glm_predict_{_sfx(X.dtype)}")(
+    getattr(lib(), f"oracle_glm_predict_{_sfx(X.dtype, bf16)}")(
         _ptr(X), _ptr(M), _ptr(Yhat), nf, nt, ntasks, nobs)
     return Yhat
 
 
-def gradient(X, M, Y, lam: float = 0.0, alpha: float = 0.0, with_reg: bool = True) -> np.ndarray:
+def gradient(X, M, Y, lam: float = 0.0, alpha: float = 0.0, with_reg: bool = True,
+             bf16: bool = False) -> np.ndarray:
     """grad = 2*sum_obs (Yhat - Y) X  [+ lam*(alpha*sign(M) + 2(1-alpha) M)].
 
     ``Y=None`` stands for an all-zero Y.
@@ -129,7 +150,7 @@ def gradient(X, M, Y, lam: float = 0.0, alpha: float = 0.0, with_reg: bool = Tru
         Y = np.ascontiguousarray(Y, dtype=X.dtype)
         assert Y.shape == (nobs, ntasks, nt), Y.shape
     grad = np.zeros((ntasks, nt, nf), dtype=X.dtype)
-    getattr(lib(), f"oracle_glm_gradient_{_sfx(X.dtype)}")(
+    getattr(lib(), f"oracle_glm_gradient_{_sfx(X.dtype, bf16)}")(
         _ptr(X), _ptr(M), _ptr(Y), _ptr(grad), nf, nt, ntasks, nobs,
         float(lam), float(alpha), int(bool(with_reg)))
     return grad
@@ -149,14 +170,14 @@ def gradient_acc64(X, M, Y, lam: float = 0.0, alpha: float = 0.0, with_reg: bool
     return grad
 
 
-def loss(M, Y, Yhat, lam: float = 0.0, alpha: float = 0.0) -> np.ndarray:
+def loss(M, Y, Yhat, lam: float = 0.0, alpha: float = 0.0, bf16: bool = False) -> np.ndarray:
     M = np.ascontiguousarray(M)
     Y = np.ascontiguousarray(Y, dtype=M.dtype)
     Yhat = np.ascontiguousarray(Yhat, dtype=M.dtype)
     ntasks, nt, nf = M.shape
     nobs = Y.shape[0]
     out = np.zeros((1,), dtype=M.dtype)
-    getattr(lib(), f"oracle_glm_loss_{_sfx(M.dtype)}")(
+    getattr(lib(), f"oracle_glm_loss_{_sfx(M.dtype, bf16)}")(
         _ptr(M), _ptr(Y), _ptr(Yhat), _ptr(out), nf, nt, ntasks, nobs, float(lam), float(alpha))
     return out
 

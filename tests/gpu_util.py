@@ -56,29 +56,31 @@ def stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def predict(X, M):
+def predict(X, M, sfx=None):
+    """``sfx`` names the C-ABI type when the dtype does not (``"bf16"`` for
+    bfloat16 bit patterns held as uint16)."""
     nobs, ntasks, nf = X.shape
     nt = M.shape[1]
     dX, dM = Dev(X), Dev(M)
     out = Dev(shape=(nobs, ntasks, nt), dtype=X.dtype)
-    capi.call(f"glmb_predict_{SFX[X.dtype]}", dX.ptr, dM.ptr, out.ptr, nf, nt, ntasks, nobs, stream())
+    capi.call(f"glmb_predict_{sfx or SFX[X.dtype]}", dX.ptr, dM.ptr, out.ptr, nf, nt, ntasks, nobs, stream())
     torch.cuda.synchronize()
     assert out.canary_intact()
     return out.numpy()
 
 
-def gradient(X, M, Y, lam=0.0, alpha=0.0, reg=True, want_yhat=False, workspace=None):
+def gradient(X, M, Y, lam=0.0, alpha=0.0, reg=True, want_yhat=False, workspace=None, sfx=None, flags=0):
     nobs, ntasks, nf = X.shape
     nt = M.shape[1]
     dX, dM = Dev(X), Dev(M)
     dY = Dev(Y) if Y is not None else None
     g = Dev(shape=(ntasks, nt, nf), dtype=X.dtype)
     yh = Dev(shape=(nobs, ntasks, nt), dtype=X.dtype) if want_yhat else None
-    flags = (capi.GRAD_REGULARIZE if reg else 0) | (capi.GRAD_WRITE_YHAT if want_yhat else 0)
+    flags |= (capi.GRAD_REGULARIZE if reg else 0) | (capi.GRAD_WRITE_YHAT if want_yhat else 0)
     if Y is None:
         flags |= capi.GRAD_Y_ZERO
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel())
-    capi.call(f"glmb_gradient_{SFX[X.dtype]}", dX.ptr, dM.ptr, dY.ptr if dY else None, g.ptr,
+    capi.call(f"glmb_gradient_{sfx or SFX[X.dtype]}", dX.ptr, dM.ptr, dY.ptr if dY else None, g.ptr,
               yh.ptr if yh else None, nf, nt, ntasks, nobs, float(lam), float(alpha), flags,
               ws_ptr, ws_bytes, stream())
     torch.cuda.synchronize()

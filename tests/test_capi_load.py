@@ -31,7 +31,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     declared = _declared_functions()
     # basics, per-type entry points, floating-point entry points, the no-allocation
     # entry point, the peer group, sharded gradient and fit, the multi-GPU context
-    assert len(declared) == 4 + 4 * 11 + 9 * 2 + 1 + 6 + 2 + 2 + 5 + 2 * 2
+    assert len(declared) == 4 + 4 * 12 + 9 * 2 + 1 + 6 + 2 + 2 + 5 + 2 * 2
     exported = _exported()
     missing = [n for n in declared if n not in exported]
     assert not missing, missing
