@@ -600,6 +600,11 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    if world > 1:
+        # device-side rendezvous: the ranks' start events are recorded once
+        # every rank's GPU has reached this all-reduce, so host launch skew
+        # after the barrier does not land in the first timed step
+        dist.all_reduce(torch.zeros(1, device=device))
 
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -695,6 +700,40 @@ def run_ours(args):
                "frac_of_h2d_ceiling": copy_ms / e2e_ms}
         del Xh, Yh, Xd, Yd
 
+    # the sharded step's two parts, each as K back-to-back calls in one graph:
+    # this rank's pass alone (rows + finalize, no exchange) and the exchange
+    # alone (the same sharded call on zero local rows); max over ranks
+    breakdown = None
+    if peer is not None and graph is not None:
+        def graph_ms(fn):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(args.steps):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            torch.cuda.synchronize()
+            dist.all_reduce(torch.zeros(1, device=device))
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            torch.cuda.synchronize()
+            del g
+            return a.elapsed_time(b) / args.steps
+
+        local_ms = graph_ms(lambda: glm.gradient(X, M, Y, w.lam, w.alpha, True, out=grad, workspace=ws))
+        X0, Y0 = X[:0], Y[:0]
+        exchange_ms = graph_ms(lambda: backend.reduced_gradient(X0, M, Y0, w.lam, w.alpha, grad, None))
+        tb = torch.tensor([local_ms, exchange_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(tb, op=dist.ReduceOp.MAX)
+        breakdown = {"local_pass_us": float(tb[0]) * 1e3, "exchange_only_us": float(tb[1]) * 1e3,
+                     "step_us": ms_per_step * 1e3,
+                     "what": "per call, K calls in one graph, max over ranks: the rank's own rows pass + "
+                             "finalize without exchange; the sharded call on zero local rows (exchange alone)"}
+
     sampler.stop()
     clocks = sampler.summary(t_wall0, t_wall1)
 
@@ -761,6 +800,8 @@ def run_ours(args):
                            "lipschitz": float(lip[0].item()), "nonzero": int((beta_fit != 0).sum().item())}
         if e2e is not None:
             line["e2e"] = e2e
+        if breakdown is not None:
+            line["breakdown"] = breakdown
         if n_gpus == 1 and not args.no_cpu_baseline:
             rows = cpu_rows(w)
             rate, cores, secs = cpu_sample_rate(w, rows)

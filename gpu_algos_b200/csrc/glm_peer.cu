@@ -143,13 +143,16 @@ __global__ void __launch_bounds__(kExThreads)
         if (lane == 0) mine[e] = s;
     }
     __syncthreads();
-    // 2. push them into the same slot of every peer's buffer
+    // 2. push them into the same slot of every peer's buffer, then raise this
+    // block's flag on every rank.  The block barrier orders every thread's
+    // stores before the flag writers' system-scope releases (release
+    // semantics are cumulative over what the barrier ordered before them),
+    // so no thread needs a fence of its own.
     for (int p = 0; p < a.world; ++p) {
         if (p == a.rank) continue;
         double* dst = slot_of(a.peers[p], parity, a.rank, a.world, a.max_elems);
         for (int64_t e = lo + tid; e < hi; e += kExThreads) dst[e] = mine[e];
     }
-    __threadfence_system();
     __syncthreads();
     if (tid < a.world) st_release_sys(flags_of(a.peers[tid], a.world, a.max_elems, a.rank, blk), epoch);
 
@@ -178,10 +181,10 @@ __global__ void __launch_bounds__(kExThreads)
         call_done(own, a.world, a.max_elems, epoch, nblk);
         return;
     }
-    // every thread acquires the flags it depends on before reading the slots
-    for (int r = 0; r < a.world; ++r) (void)ld_acquire_sys(flags_of(own, a.world, a.max_elems, r, blk));
-
-    // 4. the same rank-ordered sum on every rank, then finalize
+    // 4. the same rank-ordered sum on every rank, then finalize.  The pollers'
+    // acquires happen before the barrier above, so every thread's reads of
+    // the slots after it see the senders' stores (read through L2, never a
+    // stale L1 line).
     for (int64_t e = lo + tid; e < hi; e += kExThreads) {
         double s = 0.0;
         for (int r = 0; r < a.world; ++r) s += __ldcg(slot_of(own, parity, r, a.world, a.max_elems) + e);

@@ -124,3 +124,25 @@ def test_bf16_specials_propagate(oracle):
     assert np.array_equal(np.isnan(gf), np.isnan(of))
     assert np.array_equal(np.isinf(gf), np.isinf(of))
     assert np.array_equal(np.signbit(gf[np.isinf(gf)]), np.signbit(of[np.isinf(of)]))
+
+
+@pytest.mark.parametrize("shape,path", [((20000, 1, 128, 1), "rows"), ((700, 2, 40, 3), "rows"),
+                                        ((900, 2, 48, 12), "generic")])
+def test_bf16_logistic(shape, path):
+    """GLMB_GRAD_LOGISTIC on bfloat16: mu = sigmoid(X M) and sum (mu - Y) X
+    (+ elastic net) against float64 NumPy on the same rounded inputs, within
+    2^-7 (floor 1e-3 of the largest element); mu within 2^-7 absolute."""
+    nobs, ntasks, nf, nt = shape
+    rng = np.random.default_rng(nobs + nt)
+    X = O.bf16_bits(rng.normal(size=(nobs, ntasks, nf)) / np.sqrt(nf))
+    Xf = O.bf16_to_f32(X).astype(np.float64)
+    eta = np.einsum("otf,tkf->otk", Xf, rng.normal(size=(ntasks, nt, nf)))
+    Y = O.bf16_bits((rng.uniform(size=eta.shape) < 1 / (1 + np.exp(-eta))).astype(np.float32))
+    M = O.bf16_bits(rng.normal(size=(ntasks, nt, nf)) * 0.5)
+    Mf, Yf = O.bf16_to_f32(M).astype(np.float64), O.bf16_to_f32(Y).astype(np.float64)
+    g, mu = G.gradient(X, M, Y, 0.3, 0.4, reg=True, want_yhat=True, sfx="bf16", flags=capi.GRAD_LOGISTIC)
+    assert capi.last_path() == path
+    ref_mu = 1 / (1 + np.exp(-np.einsum("otf,tkf->otk", Xf, Mf)))
+    ref = np.einsum("otk,otf->tkf", ref_mu - Yf, Xf) + 0.3 * (0.4 * np.sign(Mf) + 2 * 0.6 * Mf)
+    assert G.rel_err(O.bf16_to_f32(g), ref, floor=1e-3 * np.abs(ref).max()) <= TOL_ORACLE
+    assert np.abs(O.bf16_to_f32(mu) - ref_mu).max() <= TOL_ORACLE

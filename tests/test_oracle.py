@@ -220,3 +220,42 @@ def test_fit_lasso_kkt_conditions(oracle):
     assert np.allclose(g[nz] + l1 * np.sign(b[nz]), 0, atol=1e-6)
     assert np.all(np.abs(g[~nz]) <= l1 + 1e-6)
     assert nz.sum() >= 3 and not nz.all()
+
+
+def test_bf16_conversions_and_hand_computed_case(oracle):
+    """bfloat16 (an input type beyond the reference's set, treated like half):
+    the NumPy conversions round to nearest even like torch's, and the oracle's
+    bfloat16 gradient of the hand-computed 2x2 case is exact (every value and
+    intermediate is representable)."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(5)
+    a = np.concatenate([rng.normal(size=20000).astype(np.float32) * 1e3,
+                        np.array([0.0, -0.0, np.inf, -np.inf, 3.0e38, 1e-40, 1.00390625, 1.01171875], np.float32)])
+    ref = torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(oracle.bf16_bits(a), ref)
+    assert np.array_equal(oracle.bf16_to_f32(ref), torch.from_numpy(ref.view(np.int16)).view(torch.bfloat16).float().numpy())
+    assert np.isnan(oracle.bf16_to_f32(oracle.bf16_bits(np.array([np.nan], np.float32))))[0]
+    X = oracle.bf16_bits(np.array([[[1.0, 2.0]], [[3.0, -1.0]]], np.float32))
+    M = oracle.bf16_bits(np.array([[[0.5, 0.0]]], np.float32))
+    Y = oracle.bf16_bits(np.array([[[1.0]], [[0.0]]], np.float32))
+    assert np.array_equal(oracle.bf16_to_f32(oracle.predict(X, M, bf16=True))[:, 0, 0], [0.5, 1.5])
+    assert np.array_equal(oracle.bf16_to_f32(oracle.gradient(X, M, Y, with_reg=False, bf16=True))[0, 0], [8.0, -5.0])
+    # lambda 0.5, alpha 0.25 (both exact in bfloat16): 8 + 0.5*(0.25 + 1.5*0.5) = 8.5
+    g = oracle.bf16_to_f32(oracle.gradient(X, M, Y, lam=0.5, alpha=0.25, bf16=True))
+    assert np.array_equal(g[0, 0], [8.5, -5.0])
+    # loss: e = [-0.5, 1.5] -> 2.5, + 0.5*(0.25*0.5 + 0.75*0.25) = 2.65625 -> bfloat16 2.65625
+    yh = oracle.predict(X, M, bf16=True)
+    assert oracle.bf16_to_f32(oracle.loss(M, Y, yh, 0.5, 0.25, bf16=True))[0] == 2.65625
+
+
+def test_bf16_gradient_within_its_rounding(oracle):
+    """float arithmetic and one rounding to bfloat16: within 2^-8 of the exact
+    gradient of the same rounded inputs, on the data's scale."""
+    rng = np.random.default_rng(6)
+    X = oracle.bf16_bits(rng.uniform(-1, 1, (3000, 2, 24)).astype(np.float32))
+    M = oracle.bf16_bits(rng.normal(size=(2, 3, 24)).astype(np.float32))
+    Y = oracle.bf16_bits(rng.normal(size=(3000, 2, 3)).astype(np.float32))
+    Xf, Mf, Yf = (oracle.bf16_to_f32(v).astype(np.float64) for v in (X, M, Y))
+    exact = 2 * np.einsum("otk,otf->tkf", np.einsum("otf,tkf->otk", Xf, Mf) - Yf, Xf)
+    g = oracle.bf16_to_f32(oracle.gradient(X, M, Y, with_reg=False, bf16=True)).astype(np.float64)
+    assert np.all(np.abs(g - exact) <= 2.0 ** -8 * (np.abs(exact) + 1e-3 * np.abs(exact).max()))
