@@ -37,6 +37,8 @@ REFERENCE_SUFFIXES = ("f16", "f32", "f64", "i8", "i16", "i32", "i64", "u8", "u16
 #: every element type of predict / gradient / loss: the reference's eleven and bfloat16
 SUFFIXES = REFERENCE_SUFFIXES + ("bf16",)
 FLOATING = ("f32", "f64")
+#: 16-bit types with the sharded entry points (partial, finalize, peer exchange) but no fit
+HALF16 = ("f16", "bf16")
 
 
 class GlmbError(RuntimeError):
@@ -94,6 +96,16 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"glmb_fit_workspace_size_{s}")
         f.argtypes = [_I64, _I64, _I64, _I64]
         f.restype = _SZ
+    for s in HALF16:
+        f = getattr(L, f"glmb_gradient_partial_{s}")
+        f.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _U32, _P, _SZ, _P]
+        f.restype = _INT
+        f = getattr(L, f"glmb_gradient_finalize_{s}")
+        f.argtypes = [_P, _P, _P, _I64, _I64, _I64, _D, _D, _U32, _P]
+        f.restype = _INT
+        f = getattr(L, f"glmb_gradient_sharded_{s}")
+        f.argtypes = [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P, _P, _SZ, _P]
+        f.restype = _INT
     L.glmb_gradient_noalloc_f32.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _D, _D, _U32, _P]
     L.glmb_gradient_noalloc_f32.restype = _INT
     L.glmb_peer_group_create.argtypes = [_INT, _INT, _I64, _D, ctypes.POINTER(ctypes.c_void_p), _P]
@@ -184,6 +196,8 @@ def exported_symbols() -> list[str]:
     names += ["glmb_peer_group_create", "glmb_peer_group_connect", "glmb_peer_group_connect_local",
               "glmb_peer_group_buffer", "glmb_peer_group_status", "glmb_peer_group_destroy"]
     names += [f"glmb_gradient_sharded_{s}" for s in FLOATING]
+    for s in HALF16:
+        names += [f"glmb_gradient_partial_{s}", f"glmb_gradient_finalize_{s}", f"glmb_gradient_sharded_{s}"]
     names += [f"glmb_fit_elastic_net_sharded_{s}" for s in FLOATING]
     names += ["glmb_mg_create", "glmb_mg_destroy", "glmb_mg_size", "glmb_mg_stream", "glmb_mg_synchronize"]
     for s in FLOATING:

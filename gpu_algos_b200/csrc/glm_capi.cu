@@ -632,4 +632,56 @@ GLMB_DEFINE_SHARDED_FIT(f64, double)
 GLMB_DEFINE_PEER(f32, float)
 GLMB_DEFINE_PEER(f64, double)
 
+// The sharded family for the 16-bit types (uint16_t bit patterns at the ABI):
+// the same partial / finalize / peer-exchange bodies on __half and bfloat16.
+#define GLMB_DEFINE_SHARDED16(SFX, NT_)                                                              \
+    int glmb_gradient_partial_##SFX(const uint16_t* X, const uint16_t* M, const uint16_t* Y, double* partial, \
+                                    uint16_t* Yhat, int64_t nf, int64_t nt, int64_t ntasks, int64_t nobs, \
+                                    uint32_t flags, void* workspace, size_t workspace_bytes,        \
+                                    glmb_stream_t stream) {                                         \
+        if (partial == nullptr && nf > 0 && nt > 0 && ntasks > 0) return GLMB_ERR_INVALID_VALUE;    \
+        return guarded([&] {                                                                        \
+            return glmb::gradient_impl<NT_>(                                                        \
+                reinterpret_cast<const NT_*>(X), reinterpret_cast<const NT_*>(M),                   \
+                reinterpret_cast<const NT_*>(Y), nullptr, reinterpret_cast<NT_*>(Yhat), partial, nf, nt, \
+                ntasks, nobs, 0.0, 0.0, flags & ~GLMB_GRAD_REGULARIZE, workspace, workspace_bytes,  \
+                reinterpret_cast<cudaStream_t>(stream));                                            \
+        });                                                                                         \
+    }                                                                                               \
+    int glmb_gradient_finalize_##SFX(const double* partial, const uint16_t* M, uint16_t* grad_M, int64_t nf, \
+                                     int64_t nt, int64_t ntasks, double lambda, double alpha,       \
+                                     uint32_t flags, glmb_stream_t stream) {                        \
+        if (nf < 0 || nt < 0 || ntasks < 0) return GLMB_ERR_INVALID_VALUE;                          \
+        const int64_t total = nf * nt * ntasks;                                                     \
+        if (total == 0) return GLMB_OK;                                                             \
+        if (partial == nullptr || M == nullptr || grad_M == nullptr) return GLMB_ERR_INVALID_VALUE; \
+        return guarded([&] {                                                                        \
+            const int st = glmb::check_device();                                                    \
+            if (st != GLMB_OK) return st;                                                           \
+            return glmb::finalize_launch<NT_, double>(partial, 1, total, reinterpret_cast<const NT_*>(M), \
+                                                      reinterpret_cast<NT_*>(grad_M), nullptr, lambda, alpha, \
+                                                      (flags & GLMB_GRAD_REGULARIZE) != 0,           \
+                                                      reinterpret_cast<cudaStream_t>(stream));      \
+        });                                                                                         \
+    }                                                                                               \
+    int glmb_gradient_sharded_##SFX(const uint16_t* X, const uint16_t* M, const uint16_t* Y, uint16_t* grad_M, \
+                                    double* partial_out, uint16_t* Yhat, int64_t nf, int64_t nt, int64_t ntasks, \
+                                    int64_t nobs, double lambda, double alpha, uint32_t flags,      \
+                                    glmb_peer_group* group, void* workspace, size_t workspace_bytes, \
+                                    glmb_stream_t stream) {                                         \
+        if (group == nullptr) return GLMB_ERR_INVALID_VALUE;                                        \
+        if (partial_out == nullptr && grad_M == nullptr && nf > 0 && nt > 0 && ntasks > 0)          \
+            return GLMB_ERR_INVALID_VALUE;                                                          \
+        return guarded([&] {                                                                        \
+            return glmb::gradient_impl<NT_>(                                                        \
+                reinterpret_cast<const NT_*>(X), reinterpret_cast<const NT_*>(M),                   \
+                reinterpret_cast<const NT_*>(Y), partial_out ? nullptr : reinterpret_cast<NT_*>(grad_M), \
+                reinterpret_cast<NT_*>(Yhat), partial_out, nf, nt, ntasks, nobs, lambda, alpha, flags, \
+                workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), group);         \
+        });                                                                                         \
+    }
+
+GLMB_DEFINE_SHARDED16(f16, __half)
+GLMB_DEFINE_SHARDED16(bf16, __nv_bfloat16)
+
 }  // extern "C"

@@ -56,12 +56,18 @@ namespace glmb {
 namespace {
 
 constexpr int kExThreads = 256;
-constexpr int kExMaxBlocks = 64;     // flags per sender
+constexpr int kExMaxBlocks = 1024;   // flags per sender
 // Target chunk: one element per warp.  The first phase (the fixed-order sum of
 // a rank's CTA partials, as glm_finalize_kernel does it) is bound by L2
 // latency, so elements are spread over warps, not walked by one (8 elements
-// per warp cost 30 us per call where one costs 4).
+// per warp cost 30 us per call where one costs 4).  The block count depends on
+// the element count alone, so every rank launches the same blocks whatever its
+// own partial count.
 constexpr int kExElemsPerBlock = kExThreads / 32;
+// At most this many partials per element: one thread sums an element's
+// partials (already reduced ones: the dense path's single partial), so large
+// gradients do not leave 31 lanes of every warp idle.
+constexpr int64_t kExThreadSumMax = 32;
 
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -132,15 +138,25 @@ __global__ void __launch_bounds__(kExThreads)
     const int parity = int(epoch & 1);
     double* mine = slot_of(own, parity, a.rank, a.world, a.max_elems);
 
-    // 1. this rank's partial for the block's elements: fixed-order sum of the CTA partials
-    for (int64_t e = lo + warp; e < hi; e += nwarps) {
-        double s = 0.0;
-        // unrolled: eight independent loads in flight, the additions in the same order
+    // 1. this rank's partial for the block's elements: fixed-order sum of the
+    // CTA partials, a warp per element when there are many, a thread per
+    // element when there are few
+    if (a.nparts > kExThreadSumMax) {
+        for (int64_t e = lo + warp; e < hi; e += nwarps) {
+            double s = 0.0;
+            // unrolled: eight independent loads in flight, the additions in the same order
 #pragma unroll 8
-        for (int64_t c = lane; c < a.nparts; c += 32) s += a.part[e * a.nparts + c];
+            for (int64_t c = lane; c < a.nparts; c += 32) s += a.part[e * a.nparts + c];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) mine[e] = s;
+            for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            if (lane == 0) mine[e] = s;
+        }
+    } else {
+        for (int64_t e = lo + tid; e < hi; e += kExThreads) {
+            double s = 0.0;
+            for (int64_t c = 0; c < a.nparts; ++c) s += a.part[e * a.nparts + c];
+            mine[e] = s;
+        }
     }
     __syncthreads();
     // 2. push them into the same slot of every peer's buffer, then raise this
@@ -304,6 +320,10 @@ int exchange_launch(glmb_peer_group* g, const double* part, int64_t nparts, int6
 
 template int exchange_launch<float>(glmb_peer_group*, const double*, int64_t, int64_t, const float*, float*, double*,
                                     double, double, bool, const int*, cudaStream_t);
+template int exchange_launch<__half>(glmb_peer_group*, const double*, int64_t, int64_t, const __half*, __half*,
+                                     double*, double, double, bool, const int*, cudaStream_t);
+template int exchange_launch<__nv_bfloat16>(glmb_peer_group*, const double*, int64_t, int64_t, const __nv_bfloat16*,
+                                            __nv_bfloat16*, double*, double, double, bool, const int*, cudaStream_t);
 template int exchange_launch<double>(glmb_peer_group*, const double*, int64_t, int64_t, const double*, double*,
                                      double*, double, double, bool, const int*, cudaStream_t);
 

@@ -109,6 +109,21 @@ struct XRegs {
         for (int v = 0; v < VEC; ++v) d = fma(m[v], D(w[v]), d);
         return d;
     }
+    // accumulators of the gradient step: one D per element
+    template <typename D>
+    using AW = D;
+    template <typename D>
+    static constexpr int AN = VEC;
+    template <typename D>
+    using RW = D;
+    template <typename D>
+    __device__ __forceinline__ static RW<D> prep(D r) {
+        return r;
+    }
+    template <typename D>
+    __device__ __forceinline__ static D acc_get(const D (&acc)[VEC], int v) {
+        return acc[v];
+    }
     template <typename D>
     __device__ __forceinline__ static void axpy(D r, const W (&w)[N], D (&acc)[VEC]) {
 #pragma unroll
@@ -145,23 +160,22 @@ __device__ __forceinline__ float fma_half16_pair(uint32_t m, uint32_t x, float d
     }
     return d;
 }
+// acc (two floats, element 2i in the low half) += rr (r in both halves) * x
 template <typename T>
-__device__ __forceinline__ void axpy_half16_pair(float r, uint32_t x, float& a0, float& a1) {
+__device__ __forceinline__ void axpy_half16_pair(uint64_t rr, uint32_t x, uint64_t& acc) {
     if constexpr (std::is_same_v<T, __half>) {
-        asm("{\n\t.reg .f16 xl, xh;\n\t.reg .f32 x0, x1;\n\t.reg .b64 a, xx, rr;\n\t"
-            "mov.b32 {xl, xh}, %3;\n\tcvt.f32.f16 x0, xl;\n\tcvt.f32.f16 x1, xh;\n\t"
-            "mov.b64 a, {%0, %1};\n\tmov.b64 xx, {x0, x1};\n\tmov.b64 rr, {%2, %2};\n\t"
-            "fma.rn.f32x2 a, rr, xx, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
-            : "+f"(a0), "+f"(a1)
-            : "f"(r), "r"(x));
+        asm("{\n\t.reg .f16 xl, xh;\n\t.reg .f32 x0, x1;\n\t.reg .b64 xx;\n\t"
+            "mov.b32 {xl, xh}, %2;\n\tcvt.f32.f16 x0, xl;\n\tcvt.f32.f16 x1, xh;\n\t"
+            "mov.b64 xx, {x0, x1};\n\tfma.rn.f32x2 %0, %1, xx, %0;\n\t}"
+            : "+l"(acc)
+            : "l"(rr), "r"(x));
     } else {
         // bfloat16 -> float is exact: the 16 bits become the high half of the float
-        asm("{\n\t.reg .b32 x0, x1;\n\t.reg .b64 a, xx, rr;\n\t"
-            "shl.b32 x0, %3, 16;\n\tand.b32 x1, %3, 0xffff0000;\n\t"
-            "mov.b64 a, {%0, %1};\n\tmov.b64 xx, {x0, x1};\n\tmov.b64 rr, {%2, %2};\n\t"
-            "fma.rn.f32x2 a, rr, xx, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
-            : "+f"(a0), "+f"(a1)
-            : "f"(r), "r"(x));
+        asm("{\n\t.reg .b32 x0, x1;\n\t.reg .b64 xx;\n\t"
+            "shl.b32 x0, %2, 16;\n\tand.b32 x1, %2, 0xffff0000;\n\t"
+            "mov.b64 xx, {x0, x1};\n\tfma.rn.f32x2 %0, %1, xx, %0;\n\t}"
+            : "+l"(acc)
+            : "l"(rr), "r"(x));
     }
 }
 template <typename T, int VEC>
@@ -201,10 +215,28 @@ struct XRegs<T, VEC> {
         for (int i = 0; i < N; ++i) d = fma_half16_pair<T>(m[i], w[i], d);
         return d;
     }
+    // accumulators: float pairs in 64-bit registers, the operands of
+    // fma.rn.f32x2; the residual is packed into both halves once per row
     template <typename D>
-    __device__ __forceinline__ static void axpy(D r, const W (&w)[N], D (&acc)[VEC]) {
+    using AW = uint64_t;
+    template <typename D>
+    static constexpr int AN = N;
+    template <typename D>
+    using RW = uint64_t;
+    template <typename D>
+    __device__ __forceinline__ static uint64_t prep(D r) {
+        const uint64_t b = __float_as_uint(r);
+        return b | (b << 32);
+    }
+    template <typename D>
+    __device__ __forceinline__ static D acc_get(const uint64_t (&acc)[N], int v) {
+        const uint64_t p = acc[v >> 1];
+        return __uint_as_float(static_cast<uint32_t>((v & 1) ? (p >> 32) : p));
+    }
+    template <typename D>
+    __device__ __forceinline__ static void axpy(uint64_t rr, const W (&w)[N], uint64_t (&acc)[N]) {
 #pragma unroll
-        for (int i = 0; i < N; ++i) axpy_half16_pair<T>(r, w[i], acc[2 * i], acc[2 * i + 1]);
+        for (int i = 0; i < N; ++i) axpy_half16_pair<T>(rr, w[i], acc[i]);
     }
 };
 template <typename T>
@@ -224,6 +256,20 @@ struct XRegs<T, 1> {
     template <typename D>
     __device__ __forceinline__ static D dot(const D (&m)[1], const W (&w)[1], D d) {
         return fma(m[0], D(half16_to_float(w[0])), d);
+    }
+    template <typename D>
+    using AW = D;
+    template <typename D>
+    static constexpr int AN = 1;
+    template <typename D>
+    using RW = D;
+    template <typename D>
+    __device__ __forceinline__ static RW<D> prep(D r) {
+        return r;
+    }
+    template <typename D>
+    __device__ __forceinline__ static D acc_get(const D (&acc)[1], int) {
+        return acc[0];
     }
     template <typename D>
     __device__ __forceinline__ static void axpy(D r, const W (&w)[1], D (&acc)[1]) {
@@ -292,8 +338,10 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
             XR::template load_m<D>(M + (task * nt + (t < nt ? t : 0)) * nf, int64_t(c * S + ls) * VEC, nf, t < nt,
                                    m[t][c]);
 
-    D acc[NT][CPL][VEC];
-    double sq = 0.0;  // LOSS: this lane's share of sum r^2
+    using AW = typename XR::template AW<D>;
+    constexpr int AN = XR::template AN<D>;
+    AW acc[NT][CPL][AN];  // zero bits: every element 0
+    double sq = 0.0;      // LOSS: this lane's share of sum r^2
     double* wsm = smem_acc + size_t(warp) * Shape::SLOTS;
     if constexpr (GRAD) {
 #pragma unroll
@@ -301,7 +349,7 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
             for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                for (int v = 0; v < VEC; ++v) acc[t][c][v] = D(0);
+                for (int i = 0; i < AN; ++i) acc[t][c][i] = AW(0);
         for (int i = lane; i < Shape::SLOTS; i += kWarp) wsm[i] = 0.0;
     }
 
@@ -311,35 +359,62 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
 #pragma unroll
         for (int t = 0; t < NT; ++t)
 #pragma unroll
-            for (int c = 0; c < CPL; ++c)
+            for (int c = 0; c < CPL; ++c) {
 #pragma unroll
                 for (int v = 0; v < VEC; ++v) {
-                    D val = acc[t][c][v];
+                    D val = XR::template acc_get<D>(acc[t][c], v);
                     if constexpr (!FULL) {
                         for (int off = S; off < kWarp; off <<= 1)
                             val += __shfl_xor_sync(0xffffffffu, val, off);
                     }
                     if (FULL || grp == 0) wsm[((t * CPL + c) * kWarp + ls) * VEC + v] += double(val);
-                    acc[t][c][v] = D(0);
                 }
+#pragma unroll
+                for (int i = 0; i < AN; ++i) acc[t][c][i] = AW(0);
+            }
     };
 
     // Issue the loads of one batch: U steps of R rows starting at `base`.
     // FULL batches load y only for the row whose residual this lane forms.
+    // Batch-invariant parts of the addresses: this lane's vectors of a row
+    // (are they inside the row?) and the distance between the batch's rows.
+    bool f_ok[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) f_ok[c] = int64_t(c * S + ls) * VEC < nf;
+    const T* x_lane = X + task * nf + int64_t(ls) * VEC;
+    const int64_t step_elems = int64_t(R) * ntasks * nf;
     auto load = [&](XW (&xb)[U][CPL][XN], D (&yb)[U][NT], int64_t base) {
+        if (base + int64_t(U - 1) * R + grp < obs_end) {
+            // every row of the batch is in range (all but a CTA's last batch):
+            // one pointer advanced by a row step, no per-row bounds
+            const T* xrow = x_lane + (base + grp) * ntasks * nf;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t obs = base + int64_t(u) * R + grp;
-            const bool ok = obs < obs_end;
-            const T* xrow = X + (obs * ntasks + task) * nf;
+            for (int u = 0; u < U; ++u) {
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) {
-                const int64_t f0 = int64_t(c * S + ls) * VEC;
-                if (ok && f0 < nf) {
-                    XR::load(xrow + f0, xb[u][c]);
-                } else {
+                for (int c = 0; c < CPL; ++c) {
+                    if (f_ok[c]) {
+                        XR::load(xrow + c * S * VEC, xb[u][c]);
+                    } else {
 #pragma unroll
-                    for (int v = 0; v < XN; ++v) xb[u][c][v] = XW(0);
+                        for (int v = 0; v < XN; ++v) xb[u][c][v] = XW(0);
+                    }
+                }
+                xrow += step_elems;
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t obs = base + int64_t(u) * R + grp;
+                const bool ok = obs < obs_end;
+                const T* xrow = x_lane + obs * ntasks * nf;
+#pragma unroll
+                for (int c = 0; c < CPL; ++c) {
+                    if (ok && f_ok[c]) {
+                        XR::load(xrow + c * S * VEC, xb[u][c]);
+                    } else {
+#pragma unroll
+                        for (int v = 0; v < XN; ++v) xb[u][c][v] = XW(0);
+                    }
                 }
             }
         }
@@ -406,9 +481,9 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                     }
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
-                        const D r = __shfl_sync(0xffffffffu, r_mine, u << (5 - LOG2U));
+                        const auto rr = XR::template prep<D>(__shfl_sync(0xffffffffu, r_mine, u << (5 - LOG2U)));
 #pragma unroll
-                        for (int c = 0; c < CPL; ++c) XR::template axpy<D>(r, xb[u][c], acc[t][c]);
+                        for (int c = 0; c < CPL; ++c) XR::template axpy<D>(rr, xb[u][c], acc[t][c]);
                     }
                 }
             }
@@ -431,8 +506,9 @@ __global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a
                         if constexpr (LOSS) {
                             if (ls == 0 && t < nt && obs < obs_end) sq = fma(double(r), double(r), sq);
                         }
+                        const auto rr = XR::template prep<D>(r);
 #pragma unroll
-                        for (int c = 0; c < CPL; ++c) XR::template axpy<D>(r, xb[u][c], acc[t][c]);
+                        for (int c = 0; c < CPL; ++c) XR::template axpy<D>(rr, xb[u][c], acc[t][c]);
                     }
                 }
             }

@@ -241,6 +241,8 @@ int glmb_gradient_noalloc_f32(const float* X, const float* M, const float* Y, fl
 
 GLMB_DECLARE_SHARDED(f32, float)
 GLMB_DECLARE_SHARDED(f64, double)
+GLMB_DECLARE_SHARDED(f16, uint16_t)
+GLMB_DECLARE_SHARDED(bf16, uint16_t)
 
 /* ------------------------------------------------------------------------
  * Sharded evaluation with the cross-GPU sum done over NVLink peer memory,
@@ -282,6 +284,8 @@ int glmb_peer_group_destroy(glmb_peer_group* group);
 
 GLMB_DECLARE_PEER(f32, float)
 GLMB_DECLARE_PEER(f64, double)
+GLMB_DECLARE_PEER(f16, uint16_t)
+GLMB_DECLARE_PEER(bf16, uint16_t)
 
 /* ------------------------------------------------------------------------
  * Elastic-net proximal gradient (ISTA).  No counterpart in the reference,

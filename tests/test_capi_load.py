@@ -30,8 +30,9 @@ def test_library_loads_and_exports_every_declared_symbol():
     L = capi.lib()
     declared = _declared_functions()
     # basics, per-type entry points, floating-point entry points, the no-allocation
-    # entry point, the peer group, sharded gradient and fit, the multi-GPU context
-    assert len(declared) == 4 + 4 * 12 + 9 * 2 + 1 + 6 + 2 + 2 + 5 + 2 * 2
+    # entry point, the peer group, sharded gradient (float/double, then the
+    # 16-bit types' partial/finalize/sharded) and fit, the multi-GPU context
+    assert len(declared) == 4 + 4 * 12 + 9 * 2 + 1 + 6 + 2 + 3 * 2 + 2 + 5 + 2 * 2
     exported = _exported()
     missing = [n for n in declared if n not in exported]
     assert not missing, missing

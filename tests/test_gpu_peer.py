@@ -31,10 +31,10 @@ def _status(g):
     return st.value
 
 
-def _sharded(g, X, M, Y, lam, alpha, partial=False):
+def _sharded(g, X, M, Y, lam, alpha, partial=False, sfx=None):
     nobs, ntasks, nf = X.shape
     nt = M.shape[1]
-    sfx = G.SFX[X.dtype]
+    sfx = sfx or G.SFX[X.dtype]
     dX, dM, dY = G.Dev(X), G.Dev(M), G.Dev(Y)
     out = G.Dev(shape=(ntasks, nt, nf), dtype=np.float64 if partial else X.dtype)
     capi.call(f"glmb_gradient_sharded_{sfx}", dX.ptr, dM.ptr, dY.ptr, None if partial else out.ptr,
@@ -62,6 +62,19 @@ def test_single_rank_group_equals_plain_gradient():
             P = _sharded(g, X, M, Y, 0.0, 0.0, partial=True)
             g0 = G.gradient(X, M, Y, reg=False)
             assert np.allclose(2 * P, g0, rtol=1e-5 if dt == np.float32 else 1e-12, atol=1e-3)
+        # the 16-bit types (bfloat16 as uint16 bit patterns)
+        for dt, sfx in ((np.float16, None), (np.uint16, "bf16")):
+            Xf = rng.uniform(-1, 1, (5000, 2, 64)) / 4
+            Mf, Yf = rng.normal(size=(2, 3, 64)), rng.normal(size=(5000, 2, 3))
+            if sfx == "bf16":
+                from oracle import pyoracle as O
+
+                X, M, Y = O.bf16_bits(Xf), O.bf16_bits(Mf), O.bf16_bits(Yf)
+            else:
+                X, M, Y = Xf.astype(dt), Mf.astype(dt), Yf.astype(dt)
+            for _ in range(2):
+                got = _sharded(g, X, M, Y, 0.3, 0.2, sfx=sfx)
+                assert np.array_equal(got, G.gradient(X, M, Y, 0.3, 0.2, sfx=sfx))
         assert _status(g) == 0
     finally:
         capi.call("glmb_peer_group_destroy", g)

@@ -162,3 +162,66 @@ def test_two_gpu_sharded_dense_and_tiles_paths(dt, exchange):
     floor = 1e-3 * np.abs(g_ref).max()
     tol = 1e-4 if dt == np.float32 else 1e-11
     assert np.max(np.abs(g0 - g_ref) / np.maximum(np.abs(g_ref), floor)) <= tol
+
+
+def _worker16(rank, world, port, outdir, dt_name, exchange):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from gpu_algos_b200.sharded import CudaBackend, PeerBackend, PeerGroup, ShardedGLM, obs_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        X, Y, M = _problem(np.float32)
+        dt = getattr(torch, dt_name)
+        lo, hi = obs_range(X.shape[0], world, rank)
+        peer = PeerGroup(max_elems=M.size, timeout_ms=5000.0) if exchange == "peer" else None
+        backend = PeerBackend(peer) if peer is not None else CudaBackend()
+        sh = ShardedGLM(torch.from_numpy(X[lo:hi].copy()).cuda().to(dt), torch.from_numpy(Y[lo:hi].copy()).cuda().to(dt),
+                        backend)
+        g = sh.gradient(torch.from_numpy(M).cuda().to(dt), 0.2, 0.3)
+        torch.cuda.synchronize()
+        if peer is not None:
+            assert peer.status() == 0
+            peer.close()
+        np.save(os.path.join(outdir, f"g{rank}.npy"), g.float().cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("dt_name", ["float16", "bfloat16"])
+def test_two_gpu_sharded_16bit_gradient(dt_name, exchange):
+    """half and bfloat16: glmb_gradient_partial/finalize (NCCL) and
+    glmb_gradient_sharded (peer exchange) on two GPUs give identical bits on
+    both ranks and match the one-GPU gradient of the full data to one unit in
+    the last place of the type (2^-10 half, 2^-7 bfloat16, relative; floor
+    1e-2 of the largest element): the partial sums are exact to float
+    precision either way, and each result is rounded once."""
+    outdir = tempfile.mkdtemp()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker16, args=(r, 2, port, outdir, dt_name, exchange)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert not p.is_alive(), "a rank hung"
+        assert p.exitcode == 0
+    from gpu_algos_b200 import glm
+
+    dt = getattr(torch, dt_name)
+    X, Y, M = _problem(np.float32)
+    tX, tY, tM = (torch.from_numpy(a).cuda().to(dt) for a in (X, Y, M))
+    g_ref = glm.gradient(tX, tM, tY, 0.2, 0.3).float().cpu().numpy().astype(np.float64)
+    g0, g1 = np.load(os.path.join(outdir, "g0.npy")), np.load(os.path.join(outdir, "g1.npy"))
+    assert np.array_equal(g0, g1)
+    tol = 2.0 ** -10 if dt_name == "float16" else 2.0 ** -7
+    den = np.maximum(np.abs(g_ref), 1e-2 * np.abs(g_ref).max())
+    assert np.max(np.abs(g0 - g_ref) / den) <= tol
