@@ -85,6 +85,9 @@ constexpr bool kRowsType = std::is_same_v<T, float> || std::is_same_v<T, double>
 // 16-byte loads)
 template <typename T>
 constexpr bool kRowsKernelType = kRowsType<T> || kHalf16<T>;
+// element types with the peer exchange (glmb_gradient_sharded_*)
+template <typename T>
+constexpr bool kPeerType = kRowsType<T> || kHalf16<T>;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -186,6 +189,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
         return GLMB_ERR_INVALID_VALUE;
     const bool logistic = (flags & GLMB_GRAD_LOGISTIC) != 0;
     if (logistic && !std::is_floating_point_v<T> && !kHalf16<T>) return GLMB_ERR_INVALID_VALUE;
+    if (peer != nullptr && !kPeerType<T>) return GLMB_ERR_UNSUPPORTED;
     const bool reg = (flags & GLMB_GRAD_REGULARIZE) != 0;
     const bool write_yhat = (flags & GLMB_GRAD_WRITE_YHAT) != 0;
     const bool y_zero = (flags & GLMB_GRAD_Y_ZERO) != 0;
@@ -232,7 +236,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
                                                         alpha, stream);
                 }
             }
-            if constexpr (kRowsType<T>) {
+            if constexpr (kPeerType<T>) {
                 if (peer != nullptr)
                     return exchange_launch<T>(peer, sc.as<double>(), p.ctas_per_task, ntasks * nt * nf, M, grad,
                                               partial_out, lambda, alpha, reg, nullptr, stream);
@@ -283,7 +287,7 @@ int gradient_impl(const T* X, const T* M, const T* Y, T* grad, T* Yhat, double* 
         }
     }
     set_last_path("generic");
-    if constexpr (kRowsType<T>) {
+    if constexpr (kPeerType<T>) {
         if (peer != nullptr) {
             PeerFinish<T> fin{peer, M, grad, partial_out, lambda, alpha, reg, nullptr, ntasks * nt * nf, stream};
             return generic_gradient<T>(X, M, Yin, grad, Yhat_out, partial_out, nf, nt, ntasks, nobs, lambda,
