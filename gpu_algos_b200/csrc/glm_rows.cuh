@@ -75,8 +75,15 @@ struct RowsShape {
     static constexpr int FPL = CPL * VEC;  // features per lane
     static constexpr int WORDS = FPL * int(sizeof(T)) / 4 + NT;
     // register words a batch may take; half rows carry half the bytes per
-    // register, so twice as many of them keep as many bytes in flight
-    static constexpr int U_RAW = (sizeof(T) == 2 ? 40 : 20) / WORDS;
+    // register, so twice as many of them keep as many bytes in flight; float
+    // rows of 16 features per lane (512 across a warp) take two rows per
+    // batch, so a warp keeps two 2 KB rows in flight rather than one
+    static constexpr bool LONG_F32 = sizeof(T) == 4 && FPL == 16 && NT == 1;
+    static constexpr int U_BUDGET = sizeof(T) == 2 ? 40 : (LONG_F32 ? 34 : 20);
+    static constexpr int U_RAW = U_BUDGET / WORDS;
+    // resident CTAs per SM the register allocation must leave room for (the
+    // two-row batches of long float rows pay off only at two CTAs per SM)
+    static constexpr int MIN_CTAS = LONG_F32 ? 2 : 1;
     // rows (or row steps) per batch: a power of two in [1, 8]
     static constexpr int U = U_RAW >= 8 ? 8 : (U_RAW >= 4 ? 4 : (U_RAW >= 2 ? 2 : 1));
     static constexpr int LOG2U = U == 8 ? 3 : (U == 4 ? 2 : (U == 2 ? 1 : 0));
@@ -289,7 +296,7 @@ struct XRegs<T, 1> {
 // before the arithmetic of batch i, so every warp keeps one batch of X in
 // flight while it computes.
 template <typename T, int VEC, int CPL, int NT, int MODE, bool FULL>
-__global__ void __launch_bounds__(kRowsThreads) glm_rows_kernel(const RowsArgs a) {
+__global__ void __launch_bounds__(kRowsThreads, RowsShape<T, VEC, CPL, NT>::MIN_CTAS) glm_rows_kernel(const RowsArgs a) {
     using D = typename Arith<T>::Dot;
     using Shape = RowsShape<T, VEC, CPL, NT>;
     using XR = XRegs<T, VEC>;
