@@ -5,23 +5,28 @@
 // the row-streaming kernel cannot hold nt x nf accumulators per lane.  Here
 // a CTA owns one (task, block of observations) and walks it in tiles of
 // kTileRows rows, two CTAs per SM (so that one CTA's block barriers overlap
-// the other's tensor work):
+// the other's tensor work).  Both contractions run on the FP64 tensor pipe
+// with the 16 x 8 x 16 double MMA (mma.sync m16n8k16 f64: 2048 multiply-adds
+// per instruction, eight times the m8n8k4 shape's):
 //
 //   1. the tile's X rows (nf doubles each) are brought into shared memory by
-//      cp.async.bulk copies completing on an mbarrier, two tiles in flight
-//      (the copy of tile i+1 overlaps the arithmetic of tile i);
-//   2. Yhat[rows, t] = X_tile . M_task^T on the FP64 tensor pipe
-//      (mma.sync m8n8k4 f64): four 8 x 8 output blocks, each computed by two
-//      warps over the two halves of K, into shared memory (the two halves are
-//      added, and y subtracted, when step 3 reads them);
-//   3. G[t, f] += r^T . X_tile, again m8n8k4 f64, G held in registers
-//      (16 x 256 doubles over 8 warps) for the CTA's whole block.
+//      cp.async.bulk copies completing on an mbarrier, into three buffers
+//      with two tiles in flight ahead of the one being processed;
+//   2. Yhat[rows, t] = X_tile . M_task^T: warp w computes the 16 rows x 8
+//      targets block (w & 1) over the K quarter (w >> 1), the model's
+//      fragments held in registers for the CTA's whole life;
+//   3. one thread per (row, target) sums the four K quarters in a fixed
+//      order, writes Yhat when asked for and r = yhat - y into shared memory;
+//   4. G[t, f] += r^T . X_tile: warp w owns features [32w, 32w + 32) (four
+//      16 x 8 blocks over all 16 targets, K = the tile's 16 rows), G held in
+//      registers for the CTA's whole block.
 //
 // X is read from HBM once; yhat and r stay on chip.  The CTA writes one
 // double per (t, f) to the partial buffer; glm_finalize_kernel reduces over
 // CTAs in a fixed order.  Every wait on an mbarrier is bounded: after
-// kWaitLimit polls the CTA records an error in the status word and stops, and
-// the host-side finalize turns that into NaN gradients (no hang).
+// kWaitLimit polls the thread records an error in the status word and waits
+// no more (no further copies are issued), and a kernel after the finalize
+// turns that into NaN gradients (no hang).  A tile costs two block barriers.
 #include <algorithm>
 #include <cstdlib>
 
@@ -32,21 +37,23 @@ namespace glmb {
 
 namespace {
 
-constexpr int kTileRows = 16;                 // observations per tile
+constexpr int kTileRows = 16;                 // observations per tile (the MMA's M for step 2, K for step 4)
 constexpr int kTileThreads = 256;             // 8 warps
 constexpr int kCtasPerSm = 2;
 constexpr int kMaxF = 256;                    // features per CTA pass
 constexpr int kMaxT = 16;                     // targets
+constexpr int kBufs = 3;                      // X tile buffers: two copies in flight
+constexpr int kMmaK = 16;                     // K of one MMA
+constexpr int kKQuarterSteps = kMaxF / 4 / kMmaK;  // MMA steps in a warp's K quarter (4)
 constexpr int kXStride = kMaxF + 4;           // padded row stride (doubles): conflict-free fragments
 constexpr int kRStride = kMaxT + 4;
 constexpr long long kWaitLimit = 1ll << 26;   // mbarrier polls before giving up
 
 struct TilesSmem {
-    double M[kMaxT][kXStride];
-    double X[2][kTileRows][kXStride];
-    double D[2][kTileRows][kRStride];  // step 2's two K halves of X_tile . M^T
-    double Ys[kTileRows][kRStride];    // the tile's y (zero outside the data)
-    unsigned long long full[2];
+    double X[kBufs][kTileRows][kXStride];
+    double D[4][kTileRows][kRStride];  // step 2's four K quarters of X_tile . M^T
+    double R[kTileRows][kRStride];     // r = yhat - y (zero outside the data)
+    unsigned long long full[kBufs];
 };
 static_assert(kCtasPerSm * (sizeof(TilesSmem) + 1024) <= 228 * 1024, "two CTAs per SM");
 
@@ -92,13 +99,18 @@ __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// D = A(8x4, row) * B(4x8, col) + C on the FP64 tensor pipe.
-// Fragments: a = A[lane/4][lane%4], b = B[lane%4][lane/4],
-// c/d = C[lane/4][(lane%4)*2 + {0,1}].
-__device__ __forceinline__ void dmma(double (&d)[2], double a, double b) {
-    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
-                 : "+d"(d[0]), "+d"(d[1])
-                 : "d"(a), "d"(b));
+// D = A(16x16, row) * B(16x8, col) + D on the FP64 tensor pipe.  With
+// g = lane / 4, q = lane % 4, the fragments are
+//   a[i] = A[g + 8 (i % 2)][q + 4 (i / 2)]   (i < 8)
+//   b[i] = B[q + 4 i][g]                      (i < 4)
+//   d[i] = D[g + 8 (i / 2)][2 q + i % 2]      (i < 4)
+__device__ __forceinline__ void dmma16(double (&d)[4], const double (&a)[8], const double (&b)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7,%8,%9,%10,%11}, "
+        "{%12,%13,%14,%15}, {%0,%1,%2,%3};"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(a[4]), "d"(a[5]), "d"(a[6]), "d"(a[7]), "d"(b[0]),
+          "d"(b[1]), "d"(b[2]), "d"(b[3]));
 }
 
 struct TilesArgs {
@@ -116,24 +128,38 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     extern __shared__ __align__(128) unsigned char smem_raw[];
     TilesSmem& sm = *reinterpret_cast<TilesSmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, q = lane & 3;
     const int64_t task = blockIdx.x / a.ctas_per_task;
     const int64_t cta = blockIdx.x - task * a.ctas_per_task;
     const int64_t obs_begin = cta * a.obs_per_cta;
     const int64_t obs_end = min(a.nobs, obs_begin + a.obs_per_cta);
     const int nf = int(a.nf), nt = int(a.nt);
-    const int kpad = (nf + 3) & ~3;  // contraction length of step 2, zero padded
     const int64_t ntasks = a.ntasks;
 
-    // model of this task, zero padded to 16 x 256; X buffers zeroed (padding
-    // columns stay zero, rows past the end contribute 0 * 0)
-    for (int i = tid; i < kMaxT * kXStride; i += kTileThreads) {
-        const int t = i / kXStride, f = i % kXStride;
-        sm.M[t][f] = (t < nt && f < nf) ? a.M[(task * nt + t) * nf + f] : 0.0;
-    }
-    for (int i = tid; i < 2 * kTileRows * kXStride; i += kTileThreads) (&sm.X[0][0][0])[i] = 0.0;
+    // step 2's assignment: targets [8 nb, 8 nb + 8), K quarter kq of the
+    // features zero padded to a multiple of 64 (ksteps MMAs of K = 16)
+    const int nb = warp & 1, kq = warp >> 1;
+    const int kpad = (nf + 63) & ~63;
+    const int ksteps = kpad / 64;
+    const int kbase = kq * (kpad / 4);
+    const bool step2 = nb * 8 < nt;
+
+    // the model's B fragments for this warp's block: M[8 nb + g][kbase + 16 s + q + 4 i]
+    double mreg[kKQuarterSteps][4];
+#pragma unroll
+    for (int s = 0; s < kKQuarterSteps; ++s)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int t = nb * 8 + g, f = kbase + kMmaK * s + q + 4 * i;
+            mreg[s][i] = (s < ksteps && t < nt && f < nf) ? a.M[(task * nt + t) * nf + f] : 0.0;
+        }
+
+    // X buffers zeroed: padding columns stay zero (they meet zero model
+    // coefficients), rows past the end of the data meet r = 0
+    for (int i = tid; i < kBufs * kTileRows * kXStride; i += kTileThreads) (&sm.X[0][0][0])[i] = 0.0;
     if (tid == 0) {
-        mbar_init(&sm.full[0], 1);
-        mbar_init(&sm.full[1], 1);
+#pragma unroll
+        for (int b = 0; b < kBufs; ++b) mbar_init(&sm.full[b], 1);
     }
     fence_proxy_async();
     __syncthreads();
@@ -142,9 +168,11 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     const uint32_t row_bytes = uint32_t(nf) * 8u;
 
     // warp 0 issues the copies of one tile: one bulk copy per row
+    bool failed = false;  // this thread's wait on a copy gave up: it waits no more
     auto issue = [&](int64_t tile) {
         if (warp != 0 || tile >= ntiles) return;
-        const int b = int(tile & 1);
+        if (__any_sync(0xffffffffu, failed)) return;
+        const int b = int(tile % kBufs);
         const int64_t base = obs_begin + tile * kTileRows;
         const int rows = int(min(int64_t(kTileRows), obs_end - base));
         if (lane == 0) mbar_arrive_expect_tx(&sm.full[b], uint32_t(rows) * row_bytes);
@@ -158,133 +186,104 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     issue(0);
     issue(1);
 
-    // G accumulators: warp w owns features [32w, 32w+32) (four 8-wide tiles)
-    // for both 8-target halves.
-    double acc[2][4][2];
+    // step 4's accumulators: G[g + 8 (i / 2)][32 warp + 8 j + 2 q + i % 2]
+    double acc[4][4];
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-        for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+    for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0;
+    const int nblocks4 = min(4, max(0, (nf - warp * 32 + 7) / 8));  // feature blocks of this warp with data
 
-    // step 2: warp w computes the 8 x 8 block (rows g1_mt, targets g1_nt)
-    // over the K half khalf
-    const int g1_mt = warp & 1, g1_nt = (warp >> 1) & 1, khalf = warp >> 2;
-    const int ksplit = (kpad / 8) * 4;  // a multiple of 4 (one DMMA step)
-    const int k_lo = khalf ? ksplit : 0, k_hi = khalf ? kpad : ksplit;
-    const int row2 = g1_mt * 8 + (lane >> 2);  // this lane's row of its block
-    bool failed = false;
-
-    // This lane's two y values of a tile (K-half-0 warps own them), loaded one
-    // tile ahead: Y streams from DRAM, and a whole tile of work hides its
-    // latency where the contraction of one tile alone did not.
-    auto load_y = [&](int64_t tile, double (&yv)[2]) {
-        const int64_t obs = obs_begin + tile * kTileRows + row2;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int t = g1_nt * 8 + (lane & 3) * 2 + i;
-            yv[i] = (khalf == 0 && a.Y != nullptr && tile < ntiles && obs < obs_end && t < nt)
-                        ? a.Y[(obs * ntasks + task) * a.nt + t]
-                        : 0.0;
-        }
+    // step 3's element: (row, target) of this thread; its y is loaded one
+    // tile ahead (Y streams from DRAM; a whole tile of work hides the latency)
+    const int r3 = tid >> 4, t3 = tid & 15;
+    auto load_y = [&](int64_t tile) -> double {
+        const int64_t obs = obs_begin + tile * kTileRows + r3;
+        return (a.Y != nullptr && tile < ntiles && obs < obs_end && t3 < nt) ? a.Y[(obs * ntasks + task) * a.nt + t3]
+                                                                            : 0.0;
     };
-    double y_cur[2], y_next[2];
-    load_y(0, y_cur);
+    double y_cur = load_y(0);
 
     for (int64_t tile = 0; tile < ntiles; ++tile) {
-        const int b = int(tile & 1);
-        load_y(tile + 1, y_next);
-        const uint32_t parity = uint32_t((tile >> 1) & 1);
-        long long polls = 0;
-        while (!mbar_try_wait(&sm.full[b], parity)) {
-            if (++polls > kWaitLimit) {
-                failed = true;
-                break;
+        const int b = int(tile % kBufs);
+        const double y_next = load_y(tile + 1);
+        const uint32_t parity = uint32_t((tile / kBufs) & 1);
+        // Every thread waits for the tile itself (no block barrier here).  A
+        // wait that runs out records the error and the thread goes on without
+        // waiting again, so every thread still reaches every block barrier;
+        // the result is overwritten with NaN afterwards.
+        if (!failed) {
+            long long polls = 0;
+            while (!mbar_try_wait(&sm.full[b], parity)) {
+                if (++polls > kWaitLimit) {
+                    failed = true;
+                    atomicExch(a.status, 1);
+                    break;
+                }
             }
-        }
-        if (__syncthreads_or(failed)) {
-            if (tid == 0) atomicExch(a.status, 1);
-            return;
         }
         const int64_t base = obs_begin + tile * kTileRows;
-        const int64_t obs2 = base + row2;
 
-        // step 2: this warp's K half of an 8 x 8 (rows x targets) block
+        // step 2: this warp's K quarter of the 16 x 8 block (rows x targets nb)
         {
-            double d[2] = {0.0, 0.0};
-            if (g1_nt * 8 < nt) {
-                // four independent accumulator chains (k mod 16)
-                double dk[4][2] = {{0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}, {0.0, 0.0}};
-                const double* xa = &sm.X[b][row2][lane & 3];
-                const double* mb = &sm.M[g1_nt * 8 + (lane >> 2)][lane & 3];
-                int k0 = k_lo;
-                for (; k0 + 16 <= k_hi; k0 += 16) {
+            double d[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};  // two chains (even/odd steps)
+            if (step2) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) dmma(dk[j], xa[k0 + 4 * j], mb[k0 + 4 * j]);
+                for (int s = 0; s < kKQuarterSteps; ++s) {
+                    if (s < ksteps) {
+                        const int k0 = kbase + kMmaK * s + q;
+                        double af[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) af[i] = sm.X[b][g + 8 * (i & 1)][k0 + 4 * (i >> 1)];
+                        dmma16(d[s & 1], af, mreg[s]);
+                    }
                 }
-#pragma unroll
-                for (int j = 0; j < 3; ++j)
-                    if (k0 + 4 * j < k_hi) dmma(dk[j], xa[k0 + 4 * j], mb[k0 + 4 * j]);
-#pragma unroll
-                for (int i = 0; i < 2; ++i) d[i] = (dk[0][i] + dk[1][i]) + (dk[2][i] + dk[3][i]);
             }
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int t = g1_nt * 8 + (lane & 3) * 2 + i;
-                const bool in = obs2 < obs_end && t < nt;
-                sm.D[khalf][row2][t] = in ? d[i] : 0.0;
-                if (khalf == 0) sm.Ys[row2][t] = in ? y_cur[i] : 0.0;
-            }
+            for (int i = 0; i < 4; ++i) sm.D[kq][g + 8 * (i >> 1)][nb * 8 + 2 * q + (i & 1)] = d[0][i] + d[1][i];
+        }
+        // every warp is past step 4 of the previous tile: its X buffer may be refilled
+        fence_proxy_async();
+        __syncthreads();
+        issue(tile + 2);
+
+        // step 3: r = yhat - y for one (row, target) per thread, quarters summed in a fixed order
+        {
+            const int64_t obs = base + r3;
+            const bool in = obs < obs_end && t3 < nt;
+            const double yhat = (sm.D[0][r3][t3] + sm.D[1][r3][t3]) + (sm.D[2][r3][t3] + sm.D[3][r3][t3]);
+            if (in && a.Yhat != nullptr) a.Yhat[(obs * ntasks + task) * a.nt + t3] = yhat;
+            sm.R[r3][t3] = in ? yhat - y_cur : 0.0;
         }
         __syncthreads();
 
-        // predictions, when asked for: one element per thread (16 x 16)
-        if (a.Yhat != nullptr) {
-            const int r = tid >> 4, t = tid & 15;
-            const int64_t obs = base + r;
-            if (obs < obs_end && t < nt)
-                a.Yhat[(obs * ntasks + task) * a.nt + t] = sm.D[0][r][t] + sm.D[1][r][t];
-        }
-
-        // step 3: G[t, f] += sum_rows r[row, t] * x[row, f], r = (D0 + D1) - y
-        const int nmt = nt > 8 ? 2 : 1;
+        // step 4: G[t, f] += sum_rows r[row, t] * x[row, f] over this warp's feature blocks
+        {
+            double af[8];
 #pragma unroll
-        for (int k0 = 0; k0 < kTileRows; k0 += 4) {
-            const int kr = k0 + (lane & 3);
-            double av[2], bv[4];
+            for (int i = 0; i < 8; ++i) af[i] = sm.R[q + 4 * (i >> 1)][g + 8 * (i & 1)];
 #pragma unroll
-            for (int mi = 0; mi < 2; ++mi) {
-                const int t = mi * 8 + (lane >> 2);
-                av[mi] = (sm.D[0][kr][t] + sm.D[1][kr][t]) - sm.Ys[kr][t];
-            }
+            for (int j = 0; j < 4; ++j) {
+                if (j < nblocks4) {
+                    const int f = warp * 32 + 8 * j + g;
+                    double bf[4];
 #pragma unroll
-            for (int ni = 0; ni < 4; ++ni) bv[ni] = sm.X[b][kr][warp * 32 + ni * 8 + (lane >> 2)];
-#pragma unroll
-            for (int mi = 0; mi < 2; ++mi) {
-                if (mi < nmt) {
-#pragma unroll
-                    for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni], av[mi], bv[ni]);
+                    for (int i = 0; i < 4; ++i) bf[i] = sm.X[b][q + 4 * i][f];
+                    dmma16(acc[j], af, bf);
                 }
             }
         }
-        __syncthreads();  // all reads of X[b], D and Ys done
-        fence_proxy_async();
-        issue(tile + 2);
-        y_cur[0] = y_next[0];
-        y_cur[1] = y_next[1];
+        y_cur = y_next;
     }
 
     // this CTA's partial: one double per (t, f)
     const int64_t K = int64_t(nt) * nf;
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int ni = 0; ni < 4; ++ni)
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int t = mi * 8 + (lane >> 2);
-                const int f = warp * 32 + ni * 8 + (lane & 3) * 2 + i;
-                if (t < nt && f < nf) a.part[(task * K + int64_t(t) * nf + f) * a.ctas_per_task + cta] = acc[mi][ni][i];
-            }
+        for (int i = 0; i < 4; ++i) {
+            const int t = g + 8 * (i >> 1);
+            const int f = warp * 32 + 8 * j + 2 * q + (i & 1);
+            if (t < nt && f < nf) a.part[(task * K + int64_t(t) * nf + f) * a.ctas_per_task + cta] = acc[j][i];
+        }
 }
 
 __global__ void tiles_poison_kernel(const int* status, double* partial_out, double* grad, int64_t n) {
