@@ -10,8 +10,8 @@
 // per instruction, eight times the m8n8k4 shape's):
 //
 //   1. the tile's X rows (nf doubles each) are brought into shared memory by
-//      cp.async.bulk copies completing on an mbarrier, into three buffers
-//      with two tiles in flight ahead of the one being processed;
+//      cp.async.bulk copies completing on an mbarrier, into three buffers;
+//      a tile's copy is issued two rounds before its step 2 runs;
 //   2. Yhat[rows, t] = X_tile . M_task^T: warp w computes the 16 rows x 8
 //      targets block (w & 1) over the K quarter (w >> 1), the model's
 //      fragments held in registers for the CTA's whole life;
@@ -21,12 +21,17 @@
 //      16 x 8 blocks over all 16 targets, K = the tile's 16 rows), G held in
 //      registers for the CTA's whole block.
 //
+// The loop is software-pipelined: one round runs step 2 of tile i+1 (four
+// MMAs in two dependent chains) and step 4 of tile i (independent MMAs)
+// between the same two block barriers, then step 3 of tile i+1, so the
+// chains' latency hides behind step 4 and a round has eight MMAs per warp.
+//
 // X is read from HBM once; yhat and r stay on chip.  The CTA writes one
 // double per (t, f) to the partial buffer; glm_finalize_kernel reduces over
 // CTAs in a fixed order.  Every wait on an mbarrier is bounded: after
 // kWaitLimit polls the thread records an error in the status word and waits
 // no more (no further copies are issued), and a kernel after the finalize
-// turns that into NaN gradients (no hang).  A tile costs two block barriers.
+// turns that into NaN gradients (no hang).
 #include <algorithm>
 #include <cstdlib>
 
@@ -185,6 +190,7 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
 
     issue(0);
     issue(1);
+    issue(2);
 
     // step 4's accumulators: G[g + 8 (i / 2)][32 warp + 8 j + 2 q + i % 2]
     double acc[4][4];
@@ -192,85 +198,107 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0;
     const int nblocks4 = min(4, max(0, (nf - warp * 32 + 7) / 8));  // feature blocks of this warp with data
 
-    // step 3's element: (row, target) of this thread; its y is loaded one
-    // tile ahead (Y streams from DRAM; a whole tile of work hides the latency)
+    // step 3's element: (row, target) of this thread; its y is loaded two
+    // tiles ahead (Y streams from DRAM; a whole tile of work hides the latency)
     const int r3 = tid >> 4, t3 = tid & 15;
     auto load_y = [&](int64_t tile) -> double {
         const int64_t obs = obs_begin + tile * kTileRows + r3;
         return (a.Y != nullptr && tile < ntiles && obs < obs_end && t3 < nt) ? a.Y[(obs * ntasks + task) * a.nt + t3]
                                                                             : 0.0;
     };
-    double y_cur = load_y(0);
 
-    for (int64_t tile = 0; tile < ntiles; ++tile) {
-        const int b = int(tile % kBufs);
-        const double y_next = load_y(tile + 1);
+    // Every thread waits for a tile's copy itself (no block barrier).  A wait
+    // that runs out records the error and the thread goes on without waiting
+    // again, so every thread still reaches every block barrier; the result is
+    // overwritten with NaN afterwards.
+    auto wait_tile = [&](int64_t tile) {
+        if (failed) return;
         const uint32_t parity = uint32_t((tile / kBufs) & 1);
-        // Every thread waits for the tile itself (no block barrier here).  A
-        // wait that runs out records the error and the thread goes on without
-        // waiting again, so every thread still reaches every block barrier;
-        // the result is overwritten with NaN afterwards.
-        if (!failed) {
-            long long polls = 0;
-            while (!mbar_try_wait(&sm.full[b], parity)) {
-                if (++polls > kWaitLimit) {
-                    failed = true;
-                    atomicExch(a.status, 1);
-                    break;
-                }
+        long long polls = 0;
+        while (!mbar_try_wait(&sm.full[tile % kBufs], parity)) {
+            if (++polls > kWaitLimit) {
+                failed = true;
+                atomicExch(a.status, 1);
+                break;
             }
         }
-        const int64_t base = obs_begin + tile * kTileRows;
+    };
+    // step 2: this warp's K quarter of the 16 x 8 block (rows x targets nb), two chains
+    auto step2_mma = [&](int64_t tile, double (&d)[2][4]) {
+        const int b = int(tile % kBufs);
+#pragma unroll
+        for (int s = 0; s < kKQuarterSteps; ++s) {
+            if (s < ksteps) {
+                const int k0 = kbase + kMmaK * s + q;
+                double af[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) af[i] = sm.X[b][g + 8 * (i & 1)][k0 + 4 * (i >> 1)];
+                dmma16(d[s & 1], af, mreg[s]);
+            }
+        }
+    };
+    auto store_d = [&](const double (&d)[2][4]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sm.D[kq][g + 8 * (i >> 1)][nb * 8 + 2 * q + (i & 1)] = d[0][i] + d[1][i];
+    };
+    // step 3: r = yhat - y for one (row, target) per thread, quarters summed in a fixed order
+    auto step3 = [&](int64_t tile, double y) {
+        const int64_t obs = obs_begin + tile * kTileRows + r3;
+        const bool in = obs < obs_end && t3 < nt;
+        const double yhat = (sm.D[0][r3][t3] + sm.D[1][r3][t3]) + (sm.D[2][r3][t3] + sm.D[3][r3][t3]);
+        if (in && a.Yhat != nullptr) a.Yhat[(obs * ntasks + task) * a.nt + t3] = yhat;
+        sm.R[r3][t3] = in ? yhat - y : 0.0;
+    };
 
-        // step 2: this warp's K quarter of the 16 x 8 block (rows x targets nb)
-        {
-            double d[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};  // two chains (even/odd steps)
-            if (step2) {
+    // step 4: G[t, f] += sum_rows r[row, t] * x[row, f] over this warp's feature blocks
+    auto step4 = [&](int64_t tile) {
+        const int b = int(tile % kBufs);
+        double af[8];
 #pragma unroll
-                for (int s = 0; s < kKQuarterSteps; ++s) {
-                    if (s < ksteps) {
-                        const int k0 = kbase + kMmaK * s + q;
-                        double af[8];
+        for (int i = 0; i < 8; ++i) af[i] = sm.R[q + 4 * (i >> 1)][g + 8 * (i & 1)];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) af[i] = sm.X[b][g + 8 * (i & 1)][k0 + 4 * (i >> 1)];
-                        dmma16(d[s & 1], af, mreg[s]);
-                    }
-                }
+        for (int j = 0; j < 4; ++j) {
+            if (j < nblocks4) {
+                const int f = warp * 32 + 8 * j + g;
+                double bf[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) bf[i] = sm.X[b][q + 4 * i][f];
+                dmma16(acc[j], af, bf);
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sm.D[kq][g + 8 * (i >> 1)][nb * 8 + 2 * q + (i & 1)] = d[0][i] + d[1][i];
         }
-        // every warp is past step 4 of the previous tile: its X buffer may be refilled
+    };
+
+    // Software pipeline over tiles: the first tile's steps 2 and 3 run ahead;
+    // then each round issues step 2 of the next tile (a dependent chain) and
+    // step 4 of this one (independent MMAs) between the same two barriers, so
+    // the chain's latency hides behind step 4.
+    if (ntiles > 0) {
+        const double y0 = load_y(0);
+        wait_tile(0);
+        double d[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
+        if (step2) step2_mma(0, d);
+        store_d(d);
+        __syncthreads();
+        step3(0, y0);
+        __syncthreads();
+    }
+    double y_cur = load_y(1);  // y of the tile whose residual step 3 forms next
+    for (int64_t tile = 0; tile < ntiles; ++tile) {
+        const bool more = tile + 1 < ntiles;  // the same in every thread
+        const double y_next = load_y(tile + 2);
+        double d[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
+        if (more) {
+            wait_tile(tile + 1);
+            if (step2) step2_mma(tile + 1, d);
+        }
+        step4(tile);
+        if (more) store_d(d);
+        // every warp is past step 4 of this tile: its X buffer may be refilled
         fence_proxy_async();
         __syncthreads();
-        issue(tile + 2);
-
-        // step 3: r = yhat - y for one (row, target) per thread, quarters summed in a fixed order
-        {
-            const int64_t obs = base + r3;
-            const bool in = obs < obs_end && t3 < nt;
-            const double yhat = (sm.D[0][r3][t3] + sm.D[1][r3][t3]) + (sm.D[2][r3][t3] + sm.D[3][r3][t3]);
-            if (in && a.Yhat != nullptr) a.Yhat[(obs * ntasks + task) * a.nt + t3] = yhat;
-            sm.R[r3][t3] = in ? yhat - y_cur : 0.0;
-        }
+        issue(tile + 3);
+        if (more) step3(tile + 1, y_cur);
         __syncthreads();
-
-        // step 4: G[t, f] += sum_rows r[row, t] * x[row, f] over this warp's feature blocks
-        {
-            double af[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) af[i] = sm.R[q + 4 * (i >> 1)][g + 8 * (i & 1)];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (j < nblocks4) {
-                    const int f = warp * 32 + 8 * j + g;
-                    double bf[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) bf[i] = sm.X[b][q + 4 * i][f];
-                    dmma16(acc[j], af, bf);
-                }
-            }
-        }
         y_cur = y_next;
     }
 
