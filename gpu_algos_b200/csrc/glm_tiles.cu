@@ -169,28 +169,56 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     fence_proxy_async();
     __syncthreads();
 
-    const int64_t ntiles = obs_end > obs_begin ? (obs_end - obs_begin + kTileRows - 1) / kTileRows : 0;
+    const int ntiles = obs_end > obs_begin ? int((obs_end - obs_begin + kTileRows - 1) / kTileRows) : 0;
     const uint32_t row_bytes = uint32_t(nf) * 8u;
 
-    // warp 0 issues the copies of one tile: one bulk copy per row
+    // Tiles are copied, waited for, and worked on in order, so every index
+    // below advances by a fixed step per tile: buffer numbers rotate
+    // 0, 1, 2, 0, ..., the copy barriers' parity flips each time the
+    // rotation wraps, and row offsets grow by 16 rows.
+
+    // copies: warp 0 issues the next tile (one bulk copy per row) into buffer ib
     bool failed = false;  // this thread's wait on a copy gave up: it waits no more
-    auto issue = [&](int64_t tile) {
-        if (warp != 0 || tile >= ntiles) return;
-        if (__any_sync(0xffffffffu, failed)) return;
-        const int b = int(tile % kBufs);
-        const int64_t base = obs_begin + tile * kTileRows;
-        const int rows = int(min(int64_t(kTileRows), obs_end - base));
-        if (lane == 0) mbar_arrive_expect_tx(&sm.full[b], uint32_t(rows) * row_bytes);
-        __syncwarp();
-        if (lane < rows) {
-            const double* src = a.X + ((base + lane) * ntasks + task) * a.nf;
-            bulk_copy_g2s(&sm.X[b][lane][0], src, row_bytes, &sm.full[b]);
+    int next_issue = 0, ib = 0;
+    auto issue_next = [&]() {
+        if (next_issue >= ntiles) return;
+        if (warp == 0 && !__any_sync(0xffffffffu, failed)) {
+            const int64_t first = obs_begin + int64_t(next_issue) * kTileRows;
+            const int rows = int(min(int64_t(kTileRows), obs_end - first));
+            if (lane == 0) mbar_arrive_expect_tx(&sm.full[ib], uint32_t(rows) * row_bytes);
+            __syncwarp();
+            if (lane < rows)
+                bulk_copy_g2s(&sm.X[ib][lane][0], a.X + ((first + lane) * ntasks + task) * a.nf, row_bytes,
+                              &sm.full[ib]);
         }
+        ++next_issue;
+        ib = ib == kBufs - 1 ? 0 : ib + 1;
     };
 
-    issue(0);
-    issue(1);
-    issue(2);
+    issue_next();
+    issue_next();
+    issue_next();
+
+    // Every thread waits for a tile's copy itself (no block barrier).  A wait
+    // that runs out records the error and the thread goes on without waiting
+    // again, so every thread still reaches every block barrier; the result is
+    // overwritten with NaN afterwards.
+    int wb = 0;
+    uint32_t wpar = 0;
+    auto wait_next = [&]() {
+        if (!failed) {
+            long long polls = 0;
+            while (!mbar_try_wait(&sm.full[wb], wpar)) {
+                if (++polls > kWaitLimit) {
+                    failed = true;
+                    atomicExch(a.status, 1);
+                    break;
+                }
+            }
+        }
+        wb = wb == kBufs - 1 ? 0 : wb + 1;
+        wpar ^= wb == 0 ? 1u : 0u;
+    };
 
     // step 4's accumulators: G[g + 8 (i / 2)][32 warp + 8 j + 2 q + i % 2]
     double acc[4][4];
@@ -198,41 +226,30 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0;
     const int nblocks4 = min(4, max(0, (nf - warp * 32 + 7) / 8));  // feature blocks of this warp with data
 
-    // step 3's element: (row, target) of this thread; its y is loaded two
-    // tiles ahead (Y streams from DRAM; a whole tile of work hides the latency)
+    // step 3's element: (row, target) of this thread.  Its y is loaded two
+    // tiles ahead (Y streams from DRAM; a whole tile of work hides the
+    // latency); y and Yhat share the offset ((obs * ntasks + task) * nt + t3).
     const int r3 = tid >> 4, t3 = tid & 15;
-    auto load_y = [&](int64_t tile) -> double {
-        const int64_t obs = obs_begin + tile * kTileRows + r3;
-        return (a.Y != nullptr && tile < ntiles && obs < obs_end && t3 < nt) ? a.Y[(obs * ntasks + task) * a.nt + t3]
-                                                                            : 0.0;
+    const bool t3_ok = t3 < nt;
+    const int rows3 = int(min(int64_t(ntiles) * kTileRows, obs_end - obs_begin)) - r3;  // this row's tiles: 16 t < rows3
+    const int64_t off3 = ((obs_begin + r3) * ntasks + task) * a.nt + t3;  // tile 0
+    const int64_t step3 = int64_t(kTileRows) * ntasks * a.nt;             // per tile
+    int y_tile = 0, r_tile = 0;
+    auto load_y_next = [&]() -> double {
+        const double v = (a.Y != nullptr && t3_ok && kTileRows * y_tile < rows3) ? a.Y[off3 + y_tile * step3] : 0.0;
+        ++y_tile;
+        return v;
     };
 
-    // Every thread waits for a tile's copy itself (no block barrier).  A wait
-    // that runs out records the error and the thread goes on without waiting
-    // again, so every thread still reaches every block barrier; the result is
-    // overwritten with NaN afterwards.
-    auto wait_tile = [&](int64_t tile) {
-        if (failed) return;
-        const uint32_t parity = uint32_t((tile / kBufs) & 1);
-        long long polls = 0;
-        while (!mbar_try_wait(&sm.full[tile % kBufs], parity)) {
-            if (++polls > kWaitLimit) {
-                failed = true;
-                atomicExch(a.status, 1);
-                break;
-            }
-        }
-    };
     // step 2: this warp's K quarter of the 16 x 8 block (rows x targets nb), two chains
-    auto step2_mma = [&](int64_t tile, double (&d)[2][4]) {
-        const int b = int(tile % kBufs);
+    auto step2_mma = [&](int b, double (&d)[2][4]) {
+        const double* xs = &sm.X[b][g][kbase + q];
 #pragma unroll
         for (int s = 0; s < kKQuarterSteps; ++s) {
             if (s < ksteps) {
-                const int k0 = kbase + kMmaK * s + q;
                 double af[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) af[i] = sm.X[b][g + 8 * (i & 1)][k0 + 4 * (i >> 1)];
+                for (int i = 0; i < 8; ++i) af[i] = xs[8 * (i & 1) * kXStride + kMmaK * s + 4 * (i >> 1)];
                 dmma16(d[s & 1], af, mreg[s]);
             }
         }
@@ -241,28 +258,27 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
 #pragma unroll
         for (int i = 0; i < 4; ++i) sm.D[kq][g + 8 * (i >> 1)][nb * 8 + 2 * q + (i & 1)] = d[0][i] + d[1][i];
     };
-    // step 3: r = yhat - y for one (row, target) per thread, quarters summed in a fixed order
-    auto step3 = [&](int64_t tile, double y) {
-        const int64_t obs = obs_begin + tile * kTileRows + r3;
-        const bool in = obs < obs_end && t3 < nt;
+    // step 3: r = yhat - y for one (row, target) per thread, quarters summed
+    // in a fixed order (tiles in order)
+    auto step3_next = [&](double y) {
+        const bool in = t3_ok && kTileRows * r_tile < rows3;
         const double yhat = (sm.D[0][r3][t3] + sm.D[1][r3][t3]) + (sm.D[2][r3][t3] + sm.D[3][r3][t3]);
-        if (in && a.Yhat != nullptr) a.Yhat[(obs * ntasks + task) * a.nt + t3] = yhat;
+        if (in && a.Yhat != nullptr) a.Yhat[off3 + r_tile * step3] = yhat;
         sm.R[r3][t3] = in ? yhat - y : 0.0;
+        ++r_tile;
     };
-
     // step 4: G[t, f] += sum_rows r[row, t] * x[row, f] over this warp's feature blocks
-    auto step4 = [&](int64_t tile) {
-        const int b = int(tile % kBufs);
+    auto step4 = [&](int b) {
+        const double* xs = &sm.X[b][q][warp * 32 + g];
         double af[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) af[i] = sm.R[q + 4 * (i >> 1)][g + 8 * (i & 1)];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             if (j < nblocks4) {
-                const int f = warp * 32 + 8 * j + g;
                 double bf[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) bf[i] = sm.X[b][q + 4 * i][f];
+                for (int i = 0; i < 4; ++i) bf[i] = xs[4 * i * kXStride + 8 * j];
                 dmma16(acc[j], af, bf);
             }
         }
@@ -272,34 +288,37 @@ __global__ void __launch_bounds__(kTileThreads, kCtasPerSm) glm_tiles_f64_kernel
     // then each round issues step 2 of the next tile (a dependent chain) and
     // step 4 of this one (independent MMAs) between the same two barriers, so
     // the chain's latency hides behind step 4.
+    int b4 = 0;  // buffer of the tile step 4 works on
     if (ntiles > 0) {
-        const double y0 = load_y(0);
-        wait_tile(0);
+        const double y0 = load_y_next();
+        wait_next();
         double d[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
         if (step2) step2_mma(0, d);
         store_d(d);
         __syncthreads();
-        step3(0, y0);
+        step3_next(y0);
         __syncthreads();
     }
-    double y_cur = load_y(1);  // y of the tile whose residual step 3 forms next
-    for (int64_t tile = 0; tile < ntiles; ++tile) {
+    double y_cur = load_y_next();  // y of the tile whose residual step 3 forms next
+    for (int tile = 0; tile < ntiles; ++tile) {
         const bool more = tile + 1 < ntiles;  // the same in every thread
-        const double y_next = load_y(tile + 2);
+        const double y_next = load_y_next();
+        const int b2 = b4 == kBufs - 1 ? 0 : b4 + 1;
         double d[2][4] = {{0.0, 0.0, 0.0, 0.0}, {0.0, 0.0, 0.0, 0.0}};
         if (more) {
-            wait_tile(tile + 1);
-            if (step2) step2_mma(tile + 1, d);
+            wait_next();
+            if (step2) step2_mma(b2, d);
         }
-        step4(tile);
+        step4(b4);
         if (more) store_d(d);
         // every warp is past step 4 of this tile: its X buffer may be refilled
         fence_proxy_async();
         __syncthreads();
-        issue(tile + 3);
-        if (more) step3(tile + 1, y_cur);
+        issue_next();  // tile + 3, into buffer b4
+        if (more) step3_next(y_cur);
         __syncthreads();
         y_cur = y_next;
+        b4 = b2;
     }
 
     // this CTA's partial: one double per (t, f)
